@@ -1,0 +1,206 @@
+/*
+ * kitty_b200.h - C ABI of the B200 (sm_100a) kernels for Kitty's quantized KV cache.
+ *
+ * Plain C: pointers, sizes and element strides only.  Every entry point
+ *   - returns KITTY_OK (0) or a KITTY_ERR_* code, with a message available
+ *     from kitty_last_error() (thread-local);
+ *   - launches asynchronously on the given CUDA stream (cudaStream_t passed as
+ *     void*, NULL = legacy default stream) and never allocates device memory;
+ *   - validates its arguments on the host before launching anything.
+ *
+ * Data layout (the reference's page pools, kitty/layout.py:128-147 in
+ * bitxwolf/kitty-kv).  P = pages, H = KV heads, D = head_dim, G = group (page)
+ * size, K = d_boost.  A "page-head" is one (page, head) slice:
+ *   key_low   [P][H][D][G/4]  u8   2-bit low plane, byte j of channel c holds
+ *                                   tokens 4j..4j+3 at bits 0,2,4,6
+ *   key_high  [P][H][K][G/4]  u8   high 2 bits of the boosted channels, row r
+ *                                   belongs to the channel with boost_idx == r
+ *   key_meta  [P][H][2][D]    f16  row 0 per-channel scale, row 1 zero-point
+ *   val_codes [P][H][G][D/4]  u8   2-bit value codes, byte j of token t holds
+ *                                   channels 4j..4j+3
+ *   val_meta  [P][H][G][2]    f16  per-token (scale, zero-point)
+ * fp16 tensors are passed as their 16-bit patterns (uint16_t / void*).
+ */
+#ifndef KITTY_B200_H_
+#define KITTY_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define KITTY_OK 0
+#define KITTY_ERR_INVALID_ARGUMENT 1 /* shape, stride, alignment or range problem */
+#define KITTY_ERR_UNSUPPORTED 2      /* valid but not implemented (e.g. head_dim not 128) */
+#define KITTY_ERR_CUDA 3             /* a CUDA runtime call failed */
+#define KITTY_ERR_WORKSPACE 4        /* workspace missing or too small */
+
+#define KITTY_ABI_VERSION 1
+
+/* ABI version compiled into the library (KITTY_ABI_VERSION). */
+int kitty_abi_version(void);
+
+/* Message describing the last error returned on the calling thread ("" if none). */
+const char* kitty_last_error(void);
+
+/* sizeof() of the argument structs below, so a foreign-function binding can
+ * check its mirror of them: kind 0 = KittyKeyQuantArgs, 1 = KittyValueQuantArgs,
+ * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs; 0 for an unknown kind. */
+size_t kitty_args_size(int kind);
+
+/* ---------------------------------------------------------------------------
+ * Key page quantisation (per channel over a G-token group; INT4 for channels
+ * with boost_idx < sentinel, INT2 otherwise; dense low plane + sparse high plane).
+ *
+ * Replaces quantize_key_page / quantize_key_page_torch
+ * (kitty/kernels/quantize_key.py:217-269 and :38-124) and the per-head loop of
+ * KittyInferencePipeline._trigger_quantization (kitty/pipeline.py:199-230).
+ * Bit-exact with the reference: scale = max(max-min, 1e-8f)/(2^b-1) in IEEE
+ * fp32, zp = clamp(rint(-min/scale), 0, 2^b-1), code = clamp(rint(x/scale)+zp),
+ * scale stored as fp16 (RN).  High-plane row boost_idx[c] receives channel c's
+ * high bits when boost_idx[c] < d_boost (rows nobody writes are zeroed; rows
+ * shared by several channels receive the OR of their bits).
+ *
+ * Job j, head h: the source element (token t, channel c) is at
+ *   key + key_off[j] + h*key_s_head + t*key_s_tok + c*key_s_ch   (fp16 elements)
+ * and the outputs go to page-head (dst_page[j], h) of the pools, whose page /
+ * head strides are given in elements (the slice itself is contiguous).
+ * ------------------------------------------------------------------------- */
+typedef struct KittyKeyQuantArgs {
+  const void* key;            /* fp16 source */
+  const int64_t* key_off;     /* [n_jobs] element offsets (device memory) */
+  int64_t key_s_head, key_s_tok, key_s_ch;
+  const uint8_t* boost_idx;   /* [H][D], unit channel stride (device memory) */
+  int64_t bidx_s_head;
+  const int32_t* dst_page;    /* [n_jobs] destination pages (device memory) */
+  uint8_t* key_low;           /* pool bases (device memory) */
+  uint8_t* key_high;
+  void* key_scale;            /* fp16; usually key_meta */
+  void* key_zero;             /* fp16; usually key_meta + D */
+  int64_t low_s_page, low_s_head;
+  int64_t high_s_page, high_s_head;
+  int64_t meta_s_page, meta_s_head;
+  int32_t n_jobs, num_heads, head_dim, group, d_boost, sentinel;
+} KittyKeyQuantArgs;
+
+int kitty_quantize_key_pages(const KittyKeyQuantArgs* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Value page quantisation (per token INT2 over D channels).
+ *
+ * Replaces quantize_value_page / quantize_value_page_torch
+ * (kitty/kernels/quantize_value.py:197-227 and :38-90) and the per-head loop of
+ * _trigger_quantization (kitty/pipeline.py:232-250), including the zero padding
+ * of a partial Value Q-buffer: tokens t >= n_valid[j] are quantised as +0.0.
+ * Scale and zero-point of token t go to val_scale/val_zero + t*meta_s_tok
+ * (meta_s_tok = 2 for the interleaved val_meta pool).
+ * ------------------------------------------------------------------------- */
+typedef struct KittyValueQuantArgs {
+  const void* value;          /* fp16 source */
+  const int64_t* value_off;   /* [n_jobs] element offsets (device memory) */
+  int64_t val_s_head, val_s_tok, val_s_ch;
+  const int32_t* n_valid;     /* [n_jobs] or NULL (= group) (device memory) */
+  const int32_t* dst_page;    /* [n_jobs] (device memory) */
+  uint8_t* val_codes;
+  void* val_scale;            /* fp16; usually val_meta */
+  void* val_zero;             /* fp16; usually val_meta + 1 */
+  int64_t codes_s_page, codes_s_head;
+  int64_t meta_s_page, meta_s_head, meta_s_tok;
+  int32_t n_jobs, num_heads, head_dim, group;
+} KittyValueQuantArgs;
+
+int kitty_quantize_value_pages(const KittyValueQuantArgs* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Key page dequantisation to fp16 (D, G) blocks: x = (code - zp) * scale in fp32,
+ * code = low | (high << 2) for channels with boost_idx < d_boost.
+ * Replaces dequantize_key_page (kitty/kernels/dequantize_key.py:169-228).
+ * Job j's output element (c, t) is at out + out_off[j] + c*out_s_ch + t*out_s_tok.
+ * Source page-head: (src_page[j], head[j]).
+ * ------------------------------------------------------------------------- */
+typedef struct KittyKeyDequantArgs {
+  const uint8_t* key_low;
+  const uint8_t* key_high;
+  const void* key_scale;
+  const void* key_zero;
+  int64_t low_s_page, low_s_head, high_s_page, high_s_head, meta_s_page, meta_s_head;
+  const int32_t* src_page;    /* [n_jobs] */
+  const int32_t* head;        /* [n_jobs] */
+  const uint8_t* boost_idx;   /* [H][D] */
+  int64_t bidx_s_head;
+  void* out;                  /* fp16 */
+  const int64_t* out_off;     /* [n_jobs] */
+  int64_t out_s_ch, out_s_tok;
+  int32_t n_jobs, num_heads, head_dim, group, d_boost;
+} KittyKeyDequantArgs;
+
+int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Fused paged GQA decode attention over the quantised pools plus the fp16
+ * regions.  For sequence b and query head qh (KV head h = qh / (Hq/H)) the keys
+ * are [sink_k (sink_len) ; pages block_table[b][0..num_pages[b]) ; tail_k
+ * (tail_len)] and the values are [sink_v ; value pages ; tail_v] in the same
+ * order; out = softmax(q.k * sm_scale) . v in fp32, stored as fp16.
+ *
+ * Replaces paged_attention / paged_attention_reference
+ * (kitty/kernels/attention.py:292-341 and :46-189, batch 1 there) with a
+ * batched form.  Key and value tails have one common length (the reference's
+ * qbuf_k / qbuf_v must be equally long, attention.py:163-165).
+ *
+ * Pools use the layout above with P = pool_pages (contiguous).  Work is split
+ * over pages ("split-K"); partial (max, sum, acc) go to the workspace and a
+ * second kernel merges them, both launched on `stream` by this call.
+ * num_splits = 0 lets the library choose.  The workspace must hold
+ * kitty_paged_decode_workspace_size() bytes for the same (batch, heads,
+ * num_splits) and be 16-byte aligned.  Concurrent calls must not share it.
+ * ------------------------------------------------------------------------- */
+typedef struct KittyDecodeArgs {
+  int32_t batch, num_q_heads, num_kv_heads, head_dim, group, d_boost;
+  float sm_scale;                     /* usually 1/sqrt(head_dim) */
+  const void* q;                      /* fp16 [B][Hq][D] (unit channel stride) */
+  int64_t q_s_seq, q_s_head;
+  void* out;                          /* fp16 [B][Hq][D] */
+  int64_t out_s_seq, out_s_head;
+  const int32_t* block_table;         /* [B][*] physical pages */
+  int64_t bt_s_seq;
+  const int32_t* num_pages;           /* [B] */
+  int64_t pool_pages;                 /* P (pages must be < P) */
+  const uint8_t* key_low;
+  const uint8_t* key_high;
+  const void* key_meta;
+  const uint8_t* val_codes;
+  const void* val_meta;
+  const uint8_t* boost_idx;           /* [H][D] */
+  int64_t bidx_s_head;
+  const void* sink_k;                 /* fp16, element (b,h,t,c) at b*s_seq+h*s_head+t*s_tok+c */
+  int64_t sk_s_seq, sk_s_head, sk_s_tok;
+  const void* sink_v;
+  int64_t sv_s_seq, sv_s_head, sv_s_tok;
+  const int32_t* sink_len;            /* [B] or NULL -> sink_len_all */
+  int32_t sink_len_all;
+  const void* tail_k;
+  int64_t tk_s_seq, tk_s_head, tk_s_tok;
+  const void* tail_v;
+  int64_t tv_s_seq, tv_s_head, tv_s_tok;
+  const int32_t* tail_len;            /* [B] or NULL -> tail_len_all */
+  int32_t tail_len_all;
+  int32_t max_pages_per_seq;          /* upper bound of num_pages[b] (host-known) */
+  int32_t num_splits;                 /* 0 = choose */
+  void* workspace;
+  size_t workspace_bytes;
+} KittyDecodeArgs;
+
+/* Bytes of workspace kitty_paged_decode needs; writes the split count it will
+ * use for these arguments to *num_splits_out (may be NULL). */
+int kitty_paged_decode_workspace_size(const KittyDecodeArgs* args, size_t* bytes, int32_t* num_splits_out);
+
+int kitty_paged_decode(const KittyDecodeArgs* args, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KITTY_B200_H_ */

@@ -1,0 +1,306 @@
+// Paged GQA decode attention, CUDA-core (FMA) variant for any shape, and the
+// split-K merge kernel shared by every decode variant.
+//
+// One CTA handles one (split, KV head, sequence).  It walks its chunk of the
+// key/value sequence - the fp16 sinks and tail (split 0 only) and the pages
+// block_table[b][split range] - keeping an online softmax (running max m,
+// running sum l, accumulator o) for each of the g = Hq/H query heads that
+// share the KV head.  Keys are dequantised exactly as the reference does,
+// (code - zp) * scale in fp32 (kitty/kernels/dequantize_key.py:89-95); values
+// likewise (kitty/kernels/quantize_value.py:121-133).  Scores are
+// (q . k) * sm_scale (kitty/kernels/attention.py:172-187).
+//
+// Per page the phases are: stage the 5 pool slices in shared memory, score
+// (thread <-> token), softmax update, accumulate (thread <-> channel).
+
+#include "kitty_decode.cuh"
+
+namespace kitty {
+namespace {
+
+constexpr int kSimtThreads = 128;
+constexpr int kMaxGroupSimt = 16;  // query heads per KV head
+
+struct SimtSmem {
+  // offsets into dynamic shared memory (bytes)
+  size_t q, kl, kh, km, vc, vm, p, row, red, stats, total;
+};
+
+__host__ __device__ inline SimtSmem simt_layout(int D, int G, int K, int g) {
+  SimtSmem s;
+  size_t o = 0;
+  auto take = [&](size_t bytes) { size_t r = o; o = (o + bytes + 15) & ~size_t(15); return r; };
+  s.q = take(size_t(g) * D * 4);
+  s.kl = take(size_t(D) * (G / 4));
+  s.kh = take(size_t(K) * (G / 4) + 4);
+  s.km = take(size_t(2) * D * 2);
+  s.vc = take(size_t(G) * (D / 4));
+  s.vm = take(size_t(G) * 2 * 2);
+  const int chunk = G > kSimtThreads ? G : kSimtThreads;
+  s.p = take(size_t(g) * chunk * 4);
+  s.row = take(size_t(D) * 4);
+  s.red = take(size_t(kSimtThreads / 32) * g * 4);
+  s.stats = take(size_t(3) * g * 4);
+  s.total = o;
+  return s;
+}
+
+__global__ void __launch_bounds__(kSimtThreads)
+decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+  extern __shared__ __align__(16) uint8_t smem[];
+  const int D = a.head_dim, G = a.group, K = a.d_boost, H = a.num_kv_heads;
+  const int g = a.num_q_heads / H;
+  const int split = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int nwarps = kSimtThreads / 32;
+  const SimtSmem L = simt_layout(D, G, K, g);
+
+  float* q_s = reinterpret_cast<float*>(smem + L.q);
+  uint8_t* kl_s = smem + L.kl;
+  uint8_t* kh_s = smem + L.kh;
+  uint16_t* km_s = reinterpret_cast<uint16_t*>(smem + L.km);
+  uint8_t* vc_s = smem + L.vc;
+  uint16_t* vm_s = reinterpret_cast<uint16_t*>(smem + L.vm);
+  float* p_s = reinterpret_cast<float*>(smem + L.p);
+  int* row_s = reinterpret_cast<int*>(smem + L.row);
+  float* red_s = reinterpret_cast<float*>(smem + L.red);
+  float* m_s = reinterpret_cast<float*>(smem + L.stats);
+  float* l_s = m_s + g;
+  float* alpha_s = l_s + g;
+  const int chunk_cap = G > kSimtThreads ? G : kSimtThreads;
+
+  const uint16_t* qg = reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq + (h * g) * a.q_s_head;
+  for (int i = tid; i < g * D; i += kSimtThreads) {
+    const int qh = i / D, c = i - qh * D;
+    q_s[i] = h2f(qg[qh * a.q_s_head + c]);
+  }
+  const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
+  for (int c = tid; c < D; c += kSimtThreads) {
+    const int r = bidx[c];
+    row_s[c] = r < K ? r : -1;
+  }
+  if (tid < g) { m_s[tid] = -INFINITY; l_s[tid] = 0.f; alpha_s[tid] = 1.f; }
+
+  // per-thread accumulators: channel c = tid + j*128 for j < ceil(D/128)
+  constexpr int kMaxChanPerThread = 2;  // D <= 256
+  float o_acc[kMaxChanPerThread][kMaxGroupSimt];
+#pragma unroll
+  for (int j = 0; j < kMaxChanPerThread; ++j)
+#pragma unroll
+    for (int qh = 0; qh < kMaxGroupSimt; ++qh) o_acc[j][qh] = 0.f;
+
+  const int npages = a.num_pages[b];
+  const int p_begin = split * plan.pages_per_split;
+  const int p_end = min(npages, p_begin + plan.pages_per_split);
+  const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
+  const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
+  const int fp16_tokens = (split == 0) ? (sink_len + tail_len) : 0;
+  const int fp16_chunks = (fp16_tokens + chunk_cap - 1) / chunk_cap;
+  const int n_items = fp16_chunks + max(0, p_end - p_begin);
+  __syncthreads();
+
+  for (int item = 0; item < n_items; ++item) {
+    const bool is_page = item >= fp16_chunks;
+    int ntok;
+    int64_t page = 0;
+    int f0 = 0;  // first fp16 token of this chunk (sinks first, then tail)
+    if (is_page) {
+      page = a.block_table[b * a.bt_s_seq + p_begin + (item - fp16_chunks)];
+      if (page < 0 || page >= a.pool_pages) continue;  // out-of-range entries are skipped
+      ntok = G;
+      // stage the five pool slices
+      const uint8_t* kl = a.key_low + (page * H + h) * (int64_t(D) * (G / 4));
+      const uint8_t* kh = a.key_high + (page * H + h) * (int64_t(K) * (G / 4));
+      const uint16_t* km = reinterpret_cast<const uint16_t*>(a.key_meta) + (page * H + h) * (2 * int64_t(D));
+      const uint8_t* vc = a.val_codes + (page * H + h) * (int64_t(G) * (D / 4));
+      const uint16_t* vm = reinterpret_cast<const uint16_t*>(a.val_meta) + (page * H + h) * (2 * int64_t(G));
+      for (int i = tid; i < D * (G / 4); i += kSimtThreads) kl_s[i] = kl[i];
+      for (int i = tid; i < K * (G / 4); i += kSimtThreads) kh_s[i] = kh[i];
+      for (int i = tid; i < 2 * D; i += kSimtThreads) km_s[i] = km[i];
+      for (int i = tid; i < G * (D / 4); i += kSimtThreads) vc_s[i] = vc[i];
+      for (int i = tid; i < 2 * G; i += kSimtThreads) vm_s[i] = vm[i];
+    } else {
+      f0 = item * chunk_cap;
+      ntok = min(chunk_cap, fp16_tokens - f0);
+    }
+    __syncthreads();
+
+    // ---- scores: thread <-> token
+    for (int t = tid; t < chunk_cap; t += kSimtThreads) {
+      float acc[kMaxGroupSimt];
+#pragma unroll
+      for (int qh = 0; qh < kMaxGroupSimt; ++qh) acc[qh] = 0.f;
+      if (t < ntok) {
+        if (is_page) {
+          const int G4 = G / 4, j = t >> 2, sh = 2 * (t & 3);
+          for (int c = 0; c < D; ++c) {
+            uint32_t code = (kl_s[c * G4 + j] >> sh) & 3u;
+            const int r = row_s[c];
+            if (r >= 0) code |= ((kh_s[r * G4 + j] >> sh) & 3u) << 2;
+            const float kv = (static_cast<float>(code) - h2f(km_s[D + c])) * h2f(km_s[c]);
+#pragma unroll
+            for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+              if (qh < g) acc[qh] = fmaf(q_s[qh * D + c], kv, acc[qh]);
+          }
+        } else {
+          const int ft = f0 + t;
+          const uint16_t* kp = (ft < sink_len)
+              ? reinterpret_cast<const uint16_t*>(a.sink_k) + b * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
+              : reinterpret_cast<const uint16_t*>(a.tail_k) + b * a.tk_s_seq + h * a.tk_s_head + (ft - sink_len) * a.tk_s_tok;
+          for (int c = 0; c < D; ++c) {
+            const float kv = h2f(kp[c]);
+#pragma unroll
+            for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+              if (qh < g) acc[qh] = fmaf(q_s[qh * D + c], kv, acc[qh]);
+          }
+        }
+      }
+#pragma unroll
+      for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+        if (qh < g) p_s[qh * chunk_cap + t] = (t < ntok) ? acc[qh] * a.sm_scale : -INFINITY;
+    }
+    __syncthreads();
+
+    // ---- online softmax update
+    for (int qh = 0; qh < g; ++qh) {
+      float mx = -INFINITY;
+      for (int t = tid; t < chunk_cap; t += kSimtThreads) mx = fmaxf(mx, p_s[qh * chunk_cap + t]);
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      if (lane == 0) red_s[warp * g + qh] = mx;
+    }
+    __syncthreads();
+    if (tid < g) {
+      float mx = m_s[tid];
+      for (int w = 0; w < nwarps; ++w) mx = fmaxf(mx, red_s[w * g + tid]);
+      alpha_s[tid] = (m_s[tid] == -INFINITY) ? 0.f : __expf(m_s[tid] - mx);
+      m_s[tid] = mx;
+    }
+    __syncthreads();
+    for (int qh = 0; qh < g; ++qh) {
+      const float mx = m_s[qh];
+      float sum = 0.f;
+      for (int t = tid; t < chunk_cap; t += kSimtThreads) {
+        const float s = p_s[qh * chunk_cap + t];
+        const float p = (s == -INFINITY) ? 0.f : __expf(s - mx);
+        p_s[qh * chunk_cap + t] = p;
+        sum += p;
+      }
+#pragma unroll
+      for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      if (lane == 0) red_s[warp * g + qh] = sum;
+    }
+    __syncthreads();
+    if (tid < g) {
+      float sum = 0.f;
+      for (int w = 0; w < nwarps; ++w) sum += red_s[w * g + tid];
+      l_s[tid] = l_s[tid] * alpha_s[tid] + sum;
+    }
+
+    // ---- accumulate: thread <-> channel
+#pragma unroll
+    for (int j = 0; j < kMaxChanPerThread; ++j) {
+      const int c = tid + j * kSimtThreads;
+      if (c >= D) break;
+      float acc[kMaxGroupSimt];
+#pragma unroll
+      for (int qh = 0; qh < kMaxGroupSimt; ++qh) acc[qh] = o_acc[j][qh] * (qh < g ? alpha_s[qh] : 0.f);
+      if (is_page) {
+        const int D4 = D / 4, jj = c >> 2, sh = 2 * (c & 3);
+        for (int t = 0; t < ntok; ++t) {
+          const uint32_t code = (vc_s[t * D4 + jj] >> sh) & 3u;
+          const float vv = (static_cast<float>(code) - h2f(vm_s[2 * t + 1])) * h2f(vm_s[2 * t]);
+#pragma unroll
+          for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+            if (qh < g) acc[qh] = fmaf(p_s[qh * chunk_cap + t], vv, acc[qh]);
+        }
+      } else {
+        for (int t = 0; t < ntok; ++t) {
+          const int ft = f0 + t;
+          const uint16_t* vp = (ft < sink_len)
+              ? reinterpret_cast<const uint16_t*>(a.sink_v) + b * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok
+              : reinterpret_cast<const uint16_t*>(a.tail_v) + b * a.tv_s_seq + h * a.tv_s_head + (ft - sink_len) * a.tv_s_tok;
+          const float vv = h2f(vp[c]);
+#pragma unroll
+          for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+            if (qh < g) acc[qh] = fmaf(p_s[qh * chunk_cap + t], vv, acc[qh]);
+        }
+      }
+#pragma unroll
+      for (int qh = 0; qh < kMaxGroupSimt; ++qh) o_acc[j][qh] = acc[qh];
+    }
+    __syncthreads();
+  }
+
+  // ---- write the partial (or final, when unsplit) result
+#pragma unroll
+  for (int j = 0; j < kMaxChanPerThread; ++j) {
+    const int c = tid + j * kSimtThreads;
+    if (c >= D) break;
+    for (int qh = 0; qh < g; ++qh) {
+      if (plan.num_splits == 1) {
+        const float l = l_s[qh];
+        uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + (h * g + qh) * a.out_s_head;
+        out[c] = f2h(l > 0.f ? o_acc[j][qh] / l : 0.f);
+      } else {
+        float* o = plan.ws_o + (((int64_t(b) * H + h) * plan.num_splits + split) * g + qh) * D;
+        o[c] = o_acc[j][qh];
+      }
+    }
+  }
+  if (plan.num_splits > 1 && tid < g) {
+    const int64_t idx = ((int64_t(b) * H + h) * plan.num_splits + split) * g + tid;
+    plan.ws_m[idx] = m_s[tid];
+    plan.ws_l[idx] = l_s[tid];
+  }
+}
+
+}  // namespace
+
+// Merge the per-split partials: out = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s.
+__global__ void decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+  const int b = blockIdx.y, qhg = blockIdx.x;  // global query head
+  const int H = a.num_kv_heads, g = a.num_q_heads / H, D = a.head_dim;
+  const int h = qhg / g, qh = qhg - h * g;
+  const int64_t base = (int64_t(b) * H + h) * plan.num_splits;
+  float M = -INFINITY;
+  for (int s = 0; s < plan.num_splits; ++s) M = fmaxf(M, plan.ws_m[(base + s) * g + qh]);
+  float L = 0.f;
+  for (int s = 0; s < plan.num_splits; ++s) {
+    const float m = plan.ws_m[(base + s) * g + qh];
+    if (m != -INFINITY) L += __expf(m - M) * plan.ws_l[(base + s) * g + qh];
+  }
+  uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + qhg * a.out_s_head;
+  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < plan.num_splits; ++s) {
+      const float m = plan.ws_m[(base + s) * g + qh];
+      if (m != -INFINITY) acc += __expf(m - M) * plan.ws_o[((base + s) * g + qh) * D + c];
+    }
+    out[c] = f2h(L > 0.f ? acc / L : 0.f);
+  }
+}
+
+int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
+  const int g = a.num_q_heads / a.num_kv_heads;
+  const SimtSmem L = simt_layout(a.head_dim, a.group, a.d_boost, g);
+  if (L.total > 200 * 1024) return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: shape needs too much shared memory");
+  if (L.total > 48 * 1024)
+    cudaFuncSetAttribute(decode_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+  dim3 grid(plan.num_splits, a.num_kv_heads, a.batch);
+  decode_simt_kernel<<<grid, kSimtThreads, L.total, stream>>>(a, plan);
+  return check_launch("decode_simt_kernel");
+}
+
+int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
+  dim3 grid(a.num_q_heads, a.batch);
+  decode_merge_kernel<<<grid, 128, 0, stream>>>(a, plan);
+  return check_launch("decode_merge_kernel");
+}
+
+bool simt_supports(const KittyDecodeArgs& a) {
+  const int g = a.num_q_heads / a.num_kv_heads;
+  return a.head_dim <= 256 && g <= kMaxGroupSimt;
+}
+
+}  // namespace kitty

@@ -1,0 +1,163 @@
+"""ctypes binding of ``libkitty_b200.so`` (the C ABI in ``include/kitty_b200.h``).
+
+The library is loaded on first use.  There is no fallback: if it is missing,
+was built for another ABI version, or a tensor is not on a CUDA device, the
+call raises ``RuntimeError``.  Every entry point is launched on the current
+torch CUDA stream of the tensors' device.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+import threading
+from pathlib import Path
+from typing import Dict, Optional, Tuple
+
+import torch
+
+ABI_VERSION = 1
+LIB_NAME = "libkitty_b200.so"
+_LIB_PATH = Path(os.environ.get("KITTY_B200_LIB", Path(__file__).resolve().parent.parent / LIB_NAME))
+
+c_i32, c_i64, c_ptr, c_f32, c_size = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
+
+KITTY_OK = 0
+ERROR_NAMES = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace"}
+
+
+class KeyQuantArgs(ctypes.Structure):
+    _fields_ = [("key", c_ptr), ("key_off", c_ptr), ("key_s_head", c_i64), ("key_s_tok", c_i64),
+                ("key_s_ch", c_i64), ("boost_idx", c_ptr), ("bidx_s_head", c_i64), ("dst_page", c_ptr),
+                ("key_low", c_ptr), ("key_high", c_ptr), ("key_scale", c_ptr), ("key_zero", c_ptr),
+                ("low_s_page", c_i64), ("low_s_head", c_i64), ("high_s_page", c_i64), ("high_s_head", c_i64),
+                ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("n_jobs", c_i32), ("num_heads", c_i32),
+                ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32), ("sentinel", c_i32)]
+
+
+class ValueQuantArgs(ctypes.Structure):
+    _fields_ = [("value", c_ptr), ("value_off", c_ptr), ("val_s_head", c_i64), ("val_s_tok", c_i64),
+                ("val_s_ch", c_i64), ("n_valid", c_ptr), ("dst_page", c_ptr), ("val_codes", c_ptr),
+                ("val_scale", c_ptr), ("val_zero", c_ptr), ("codes_s_page", c_i64), ("codes_s_head", c_i64),
+                ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("meta_s_tok", c_i64), ("n_jobs", c_i32),
+                ("num_heads", c_i32), ("head_dim", c_i32), ("group", c_i32)]
+
+
+class KeyDequantArgs(ctypes.Structure):
+    _fields_ = [("key_low", c_ptr), ("key_high", c_ptr), ("key_scale", c_ptr), ("key_zero", c_ptr),
+                ("low_s_page", c_i64), ("low_s_head", c_i64), ("high_s_page", c_i64), ("high_s_head", c_i64),
+                ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("src_page", c_ptr), ("head", c_ptr),
+                ("boost_idx", c_ptr), ("bidx_s_head", c_i64), ("out", c_ptr), ("out_off", c_ptr),
+                ("out_s_ch", c_i64), ("out_s_tok", c_i64), ("n_jobs", c_i32), ("num_heads", c_i32),
+                ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32)]
+
+
+class DecodeArgs(ctypes.Structure):
+    _fields_ = [("batch", c_i32), ("num_q_heads", c_i32), ("num_kv_heads", c_i32), ("head_dim", c_i32),
+                ("group", c_i32), ("d_boost", c_i32), ("sm_scale", c_f32),
+                ("q", c_ptr), ("q_s_seq", c_i64), ("q_s_head", c_i64),
+                ("out", c_ptr), ("out_s_seq", c_i64), ("out_s_head", c_i64),
+                ("block_table", c_ptr), ("bt_s_seq", c_i64), ("num_pages", c_ptr), ("pool_pages", c_i64),
+                ("key_low", c_ptr), ("key_high", c_ptr), ("key_meta", c_ptr), ("val_codes", c_ptr),
+                ("val_meta", c_ptr), ("boost_idx", c_ptr), ("bidx_s_head", c_i64),
+                ("sink_k", c_ptr), ("sk_s_seq", c_i64), ("sk_s_head", c_i64), ("sk_s_tok", c_i64),
+                ("sink_v", c_ptr), ("sv_s_seq", c_i64), ("sv_s_head", c_i64), ("sv_s_tok", c_i64),
+                ("sink_len", c_ptr), ("sink_len_all", c_i32),
+                ("tail_k", c_ptr), ("tk_s_seq", c_i64), ("tk_s_head", c_i64), ("tk_s_tok", c_i64),
+                ("tail_v", c_ptr), ("tv_s_seq", c_i64), ("tv_s_head", c_i64), ("tv_s_tok", c_i64),
+                ("tail_len", c_ptr), ("tail_len_all", c_i32),
+                ("max_pages_per_seq", c_i32), ("num_splits", c_i32),
+                ("workspace", c_ptr), ("workspace_bytes", c_size)]
+
+
+# Every symbol the header declares, with its ctypes signature.
+SIGNATURES = {
+    "kitty_abi_version": (ctypes.c_int, []),
+    "kitty_last_error": (ctypes.c_char_p, []),
+    "kitty_args_size": (c_size, [ctypes.c_int]),
+    "kitty_quantize_key_pages": (ctypes.c_int, [ctypes.POINTER(KeyQuantArgs), c_ptr]),
+    "kitty_quantize_value_pages": (ctypes.c_int, [ctypes.POINTER(ValueQuantArgs), c_ptr]),
+    "kitty_dequantize_key_pages": (ctypes.c_int, [ctypes.POINTER(KeyDequantArgs), c_ptr]),
+    "kitty_paged_decode_workspace_size": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(c_size),
+                                                         ctypes.POINTER(c_i32)]),
+    "kitty_paged_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
+}
+STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs}
+
+_lib: Optional[ctypes.CDLL] = None
+_lock = threading.Lock()
+
+
+def library_path() -> Path:
+    return _LIB_PATH
+
+
+def load() -> ctypes.CDLL:
+    """Load the library (once), bind every signature and check the ABI."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        if not _LIB_PATH.exists():
+            raise RuntimeError(
+                f"Kitty CUDA library not found at {_LIB_PATH}. Build it with "
+                "`python kitty-kv_b200/build.py` (there is no CPU fallback).")
+        lib = ctypes.CDLL(str(_LIB_PATH))
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        if lib.kitty_abi_version() != ABI_VERSION:
+            raise RuntimeError(f"{_LIB_PATH} has ABI version {lib.kitty_abi_version()}, expected {ABI_VERSION}")
+        for kind, st in STRUCTS.items():
+            if lib.kitty_args_size(kind) != ctypes.sizeof(st):
+                raise RuntimeError(f"struct layout mismatch for {st.__name__}: library "
+                                   f"{lib.kitty_args_size(kind)} bytes, binding {ctypes.sizeof(st)}")
+        _lib = lib
+        return lib
+
+
+def check(rc: int, what: str) -> None:
+    if rc != KITTY_OK:
+        msg = load().kitty_last_error().decode(errors="replace")
+        raise RuntimeError(f"{what} failed ({ERROR_NAMES.get(rc, rc)}): {msg}")
+
+
+def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("Kitty B200 kernels need CUDA tensors (there is no CPU path); "
+                               f"got a tensor on {t.device}")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise RuntimeError(f"tensors on different devices: {dev} and {t.device}")
+    if dev is None:
+        raise RuntimeError("no CUDA tensor given")
+    return dev
+
+
+def stream_ptr(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def ptr(t: Optional[torch.Tensor]) -> int:
+    return 0 if t is None else t.data_ptr()
+
+
+# Small per-device constant tensors reused by single-page calls (no per-call allocation).
+_consts: Dict[Tuple[torch.device, str], torch.Tensor] = {}
+
+
+def zeros_const(device: torch.device, dtype: torch.dtype, n: int = 1) -> torch.Tensor:
+    key = (device, f"{dtype}:{n}")
+    t = _consts.get(key)
+    if t is None:
+        t = torch.zeros(n, dtype=dtype, device=device)
+        _consts[key] = t
+    return t

@@ -1,0 +1,245 @@
+"""CPU tests of the host-side mirror of the reference API: config, layout manager
+(allocation policy, pools, accessors, block tables), the pipeline state machine
+(with the two quantise launches replaced by a recorder, since the kernels need
+a GPU) and the sensitivity profiler.  Behaviour follows the reference's own
+tests (tests/test_layout.py, tests/test_attention.py, tests/test_quantize.py)."""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import kitty
+from kitty import pipeline as pipeline_mod
+from kitty.config import KittyConfig
+from kitty.layout import PageCentricKVLayoutManager
+from kitty.pipeline import KittyInferencePipeline
+from kitty.sensitivity import KittySensitivityProfiler, _ChannelAccumulator
+from oracle import kitty_oracle as O
+
+
+def cfg(**kw):
+    d = dict(num_layers=1, num_kv_heads=2, head_dim=16, q_buffer_size=8, sink_size=4, local_value_window=8,
+             boost_rate=0.25, device="cpu")
+    d.update(kw)
+    return KittyConfig(**d)
+
+
+def bidx_for(c):
+    b = torch.full((c.num_layers, c.num_kv_heads, c.head_dim), c.sentinel, dtype=torch.uint8)
+    b[:, :, :c.d_boost] = torch.arange(c.d_boost, dtype=torch.uint8)
+    return b
+
+
+# ----------------------------------------------------------------- config
+
+def test_config_derived_values_and_io(tmp_path):
+    c = KittyConfig(device="cpu")
+    assert c.d_boost == 16 and c.sentinel == 17
+    assert c.max_pages == ((32768 - 32) // 128 + 2) * 1 == 257
+    p = KittyConfig.kitty_pro(device="cpu")
+    assert p.d_boost == 32 and p.variant == "kitty-pro"
+    c.save(tmp_path / "c.json")
+    assert KittyConfig.load(tmp_path / "c.json") == c
+    with pytest.raises(AssertionError):
+        KittyConfig(boost_rate=1.0)
+    with pytest.raises(AssertionError):
+        KittyConfig(head_dim=18)
+    with pytest.raises(AssertionError):
+        KittyConfig(q_buffer_size=6)
+    assert "d_boost=16" in repr(c)
+
+
+def test_public_api_names():
+    for n in ["KittyConfig", "KittySensitivityProfiler", "PageCentricKVLayoutManager", "KittyInferencePipeline",
+              "KittyPagedAttention", "KittyAttentionFactory"]:
+        assert hasattr(kitty, n)
+    from kitty import kernels
+    for n in ["quantize_key_page", "quantize_key_page_torch", "dequantize_key_page", "dequantize_key_page_torch",
+              "quantize_value_page", "quantize_value_page_torch", "dequantize_value_page_torch", "paged_attention",
+              "paged_attention_reference", "paged_attention_batched", "quantize_key_pages", "quantize_value_pages"]:
+        assert callable(getattr(kernels, n))
+
+
+def test_kernels_reject_cpu_tensors():
+    from kitty import kernels
+    with pytest.raises(RuntimeError, match="CUDA"):
+        kernels.quantize_value_page_torch(torch.zeros(8, 16, dtype=torch.float16))
+
+
+# ----------------------------------------------------------------- layout
+
+def test_pool_shapes_and_dtypes():
+    c = cfg()
+    lay = PageCentricKVLayoutManager(c, bidx_for(c))
+    P, H, D, G, K = c.max_pages, c.num_kv_heads, c.head_dim, c.q_buffer_size, c.d_boost
+    assert lay.key_baseline.shape == (P, H, D, G // 4) and lay.key_baseline.dtype == torch.uint8
+    assert lay.key_boost.shape == (P, H, K, G // 4)
+    assert lay.key_metadata.shape == (P, H, 2, D) and lay.key_metadata.dtype == torch.float16
+    assert lay.value_pool.shape == (P, H, G, D // 4)
+    assert lay.value_metadata.shape == (P, H, G, 2)
+    assert lay.key_baseline_page(0).shape == (H, D, G // 4)
+    assert lay.key_boost_page(0).shape == (H, K, G // 4)
+    assert lay.key_meta_page(0).shape == (H, 2, D)
+    assert lay.value_page(0).shape == (H, G, D // 4)
+    assert lay.value_meta_page(0).shape == (H, G, 2)
+
+
+def test_allocation_policy_matches_reference():
+    c = cfg()
+    lay = PageCentricKVLayoutManager(c, bidx_for(c))
+    pages = [lay.allocate_page(0, 0, i) for i in range(5)]
+    assert [p.physical_idx for p in pages] == [0, 1, 2, 3, 4]
+    lay.free_page(0, 0, 1)
+    lay.free_page(0, 0, 3)
+    assert lay.allocate_page(1, 0, 0).physical_idx == 1          # lowest free first
+    assert lay.allocate_page(1, 0, 1).physical_idx == 3
+    assert lay.allocate_page(1, 0, 2).physical_idx == 5
+    assert lay.get_page_list(1, 0) == [1, 3, 5]
+    assert lay.get_page_list(0, 0) == [0]                        # stops at the gap (page 1 freed)
+    assert lay.get_physical_idx(0, 0, 2) == 2
+    with pytest.raises(KeyError):
+        lay.get_physical_idx(9, 0, 0)
+    lay.free_sequence(1)
+    assert lay.memory_stats()["pages_used"] == 3
+    lay.free_page(5, 5, 5)                                        # unknown page: no-op
+
+
+def test_pool_exhaustion_raises():
+    c = cfg()
+    lay = PageCentricKVLayoutManager(c, bidx_for(c))
+    for i in range(c.max_pages):
+        lay.allocate_page(0, 0, i)
+    with pytest.raises(RuntimeError, match="exhausted"):
+        lay.allocate_page(0, 0, c.max_pages)
+
+
+def test_block_table():
+    c = cfg()
+    lay = PageCentricKVLayoutManager(c, bidx_for(c))
+    for i in range(3):
+        lay.allocate_page(0, 0, i)
+    for i in range(2):
+        lay.allocate_page(4, 0, i)
+    bt, n = lay.block_table([4, 0, 9], 0, width=4)
+    assert bt.tolist() == [[3, 4, 0, 0], [0, 1, 2, 0], [0, 0, 0, 0]]
+    assert n.tolist() == [2, 3, 0]
+    with pytest.raises(RuntimeError):
+        lay.block_table([0], 0, width=2)
+
+
+# ----------------------------------------------------------------- pipeline
+
+class Recorder:
+    """Stands in for the two quantise launches: records what the flush passes."""
+
+    def __init__(self):
+        self.key_calls, self.value_calls = [], []
+
+    def key(self, src, offs, strides, bidx, K, sent, dst, kl, kh, km, H, D, G):
+        self.key_calls.append(dict(src=src.clone(), strides=strides, dst=dst.clone(), K=K, sent=sent,
+                                   bidx=bidx.clone()))
+
+    def value(self, src, offs, strides, dst, vc, vm, H, D, G, n_valid=None):
+        self.value_calls.append(dict(src=src.clone(), dst=dst.clone(),
+                                     n_valid=None if n_valid is None else int(n_valid[0])))
+
+
+@pytest.fixture
+def recorder(monkeypatch):
+    r = Recorder()
+    monkeypatch.setattr(pipeline_mod, "quantize_key_pages", r.key)
+    monkeypatch.setattr(pipeline_mod, "quantize_value_pages", r.value)
+    return r
+
+
+def make_pipe(c, align=True):
+    lay = PageCentricKVLayoutManager(c, bidx_for(c))
+    return KittyInferencePipeline(c, lay, bidx_for(c), align_values=align), lay
+
+
+def tok(i, H=2, D=16):
+    return torch.full((H, D), float(i), dtype=torch.float16)
+
+
+def test_sink_then_qbuf(recorder):
+    c = cfg()
+    p, lay = make_pipe(c)
+    for t in range(c.sink_size):
+        p.push_token(0, tok(t), tok(-t))
+    assert p.sink_fill == 4 and p.key_qbuf_len == 0
+    for t in range(3):
+        p.push_token(0, tok(10 + t), tok(20 + t))
+    assert p.key_qbuf_len == 3 and p.val_local_len == 3
+    assert not recorder.key_calls
+
+
+@pytest.mark.parametrize("align", [True, False])
+def test_flush_at_G_and_sources(recorder, align):
+    c = cfg()
+    p, lay = make_pipe(c, align)
+    n = c.sink_size + 3 * c.q_buffer_size + 2
+    for t in range(n):
+        p.push_token(0, tok(t), tok(1000 + t))
+    assert len(recorder.key_calls) == 3 and len(recorder.value_calls) == 3
+    assert lay.get_page_list(0, 0) == [0, 1, 2]
+    assert p.key_qbuf_len == 2
+    G, S, R = c.q_buffer_size, c.sink_size, c.local_value_window
+    for i, call in enumerate(recorder.key_calls):
+        assert int(call["dst"][0]) == i
+        toks = call["src"][0, :, 0].float().tolist()                # (H, G, D) buffer, head 0, channel 0
+        assert toks == [float(S + i * G + j) for j in range(G)]
+    for i, call in enumerate(recorder.value_calls):
+        vals = call["src"][0, :, 0].float().tolist()
+        if align:
+            assert call["n_valid"] is None
+            assert vals == [float(1000 + S + i * G + j) for j in range(G)]   # same tokens as key page i
+        else:
+            # reference order: evicted values; page 0 is all padding when R == G
+            nv = call["n_valid"]
+            assert nv == (0 if i == 0 else G)
+            if i > 0:
+                assert vals == [float(1000 + S + (i - 1) * G + j) for j in range(G)]
+    ctx = p.get_attention_context(0)
+    assert ctx["key_qbuf"].shape == (2, 2, 16)
+    assert ctx["page_list"] == [0, 1, 2]
+    if align:
+        assert ctx["value_tail"][0, :, 0].float().tolist() == [1000.0 + n - 2, 1000.0 + n - 1]
+    assert ctx["val_local"].shape[1] == R
+
+
+def test_reset_and_per_layer_counters(recorder):
+    c = cfg(num_layers=2)
+    p, lay = make_pipe(c)
+    for t in range(c.sink_size + c.q_buffer_size):
+        for l in range(2):
+            p.push_token(l, tok(t + 100 * l), tok(t))
+    assert len(recorder.key_calls) == 2                              # one flush per layer
+    assert lay.get_page_list(0, 0) == [0] and lay.get_page_list(0, 1) == [1]
+    # layer 1 wrote its own tokens at the same positions as layer 0
+    assert p.sink_k[1, 0, :, 0].tolist() == [100.0 + t for t in range(c.sink_size)]
+    assert recorder.key_calls[1]["src"][0, :, 0].tolist() == [100.0 + c.sink_size + j for j in range(8)]
+    assert p.layer_state(1) == p.layer_state(0)
+    p.reset_sequence(0)
+    assert p.sink_fill == 0 and p.key_qbuf_len == 0 and lay.memory_stats()["pages_used"] == 0
+    assert p.stats()["pages_used"] == 0
+
+
+# ----------------------------------------------------------------- profiler
+
+def test_profiler_compute_matches_oracle_rule():
+    c = KittyConfig(num_layers=2, num_kv_heads=4, head_dim=32, boost_rate=0.25, device="cpu")
+    prof = KittySensitivityProfiler(c)
+    rng = np.random.default_rng(0)
+    keys = []
+    for l in range(2):
+        k = (rng.standard_normal((1, 4, 50, 32)) * rng.uniform(0.1, 5, (1, 4, 1, 32))).astype(np.float32)
+        acc = _ChannelAccumulator(4, 32, "cpu")
+        acc.update(torch.from_numpy(k))
+        prof._accumulators[l] = acc
+        keys.append(k[0])
+    prof.compute()
+    exp = np.stack([O.boost_idx_from_scores(np.abs(k).mean(axis=1), c.d_boost, c.sentinel) for k in keys])
+    np.testing.assert_array_equal(prof.boost_idx_uint8.numpy(), exp)
+    assert prof.boost_masks.sum().item() == 2 * 4 * c.d_boost
