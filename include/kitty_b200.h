@@ -199,6 +199,12 @@ int kitty_paged_decode_workspace_size(const KittyDecodeArgs* args, size_t* bytes
 
 int kitty_paged_decode(const KittyDecodeArgs* args, void* stream);
 
+/* Sticky error bits set by device code on the current device (bit 0: a decode
+ * kernel gave up waiting for a bulk copy after its bounded wait and returned
+ * without a valid result).  Synchronises with the device; clear != 0 resets the
+ * bits after reading them. */
+int kitty_device_error_flags(uint32_t* flags, int clear);
+
 #ifdef __cplusplus
 }
 #endif

@@ -121,6 +121,12 @@ int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream) {
   return dequantize_key_pages_impl(args, stream);
 }
 
+int kitty_device_error_flags(uint32_t* flags, int clear) {
+  clear_error();
+  if (!flags) return fail(KITTY_ERR_INVALID_ARGUMENT, "device_error_flags: flags is NULL");
+  return read_decode_error(flags, clear);
+}
+
 int kitty_paged_decode_workspace_size(const KittyDecodeArgs* args, size_t* bytes, int32_t* num_splits_out) {
   clear_error();
   int rc = validate_decode(args);

@@ -24,5 +24,6 @@ int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaSt
 bool simt_supports(const KittyDecodeArgs& a);
 bool mma_supports(const KittyDecodeArgs& a);
 int mma_ctas_per_sm();
+int read_decode_error(uint32_t* flags, int clear);
 
 }  // namespace kitty

@@ -7,10 +7,10 @@
 // (__fdiv_rn), rounding is half-to-even (rintf), and the stored scale is the
 // float32 scale rounded to fp16.  The packed planes are therefore bit-exact.
 //
-// One CTA handles one page-head: it stages the G x D fp16 block in shared
-// memory with coalesced 16-byte loads (the block is 32 KB at D = G = 128),
-// reduces per channel (keys) or per token (values), then quantises and packs
-// four 2-bit codes per byte straight into the pool slice.
+// One CTA handles one page-head.  The general kernels stage the G x D fp16
+// block in shared memory, reduce per channel (keys) or per token (values),
+// then quantise and pack four 2-bit codes per byte into the pool slice; the
+// D = G = 128 kernels keep the block in registers (see below).
 
 #include "kitty_common.cuh"
 
@@ -221,6 +221,218 @@ __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// D = G = 128 fast paths.  256 threads: thread (tg = tid >> 4, cg = tid & 15)
+// holds tokens 8*tg .. 8*tg+7 x channels 8*cg .. 8*cg+7 of the page-head in
+// registers (eight 16-byte loads, coalesced: a half-warp reads one 256-byte
+// token row).  Min / max are taken on packed halves (exact, NaN-propagating),
+// the statistics follow the reference's float32 sequence, and the packed
+// planes are staged in shared memory so every global store is 16 bytes wide.
+// ---------------------------------------------------------------------------
+
+constexpr int kFastThreads = 256;
+
+struct Tile8x8 {
+  uint4 row[8];  // row[i] = 8 channels (fp16) of token 8*tg + i
+};
+
+// The job offset comes from device memory, so 16-byte alignment of the rows is
+// checked here (uniform per CTA); unaligned sources take 16-bit loads.
+__device__ __forceinline__ void load_tile(Tile8x8& t, const uint16_t* src, int64_t s_tok, int tg, int cg,
+                                          int n_valid) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int tok = 8 * tg + i;
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (tok < n_valid) {
+      const uint16_t* p = src + tok * s_tok + 8 * cg;
+      if (vec) {
+        v = *reinterpret_cast<const uint4*>(p);
+      } else {
+        v.x = uint32_t(p[0]) | (uint32_t(p[1]) << 16); v.y = uint32_t(p[2]) | (uint32_t(p[3]) << 16);
+        v.z = uint32_t(p[4]) | (uint32_t(p[5]) << 16); v.w = uint32_t(p[6]) | (uint32_t(p[7]) << 16);
+      }
+    }
+    t.row[i] = v;
+  }
+}
+
+__device__ __forceinline__ __half2 u2h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
+__device__ __forceinline__ uint32_t h22u(__half2 x) { return *reinterpret_cast<uint32_t*>(&x); }
+
+__device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
+  return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
+}
+
+// code of x (fp32 of an fp16) with the reference's arithmetic; fast clamps when the
+// channel / token statistics are finite (then every element is finite too)
+__device__ __forceinline__ uint32_t quant_code(float x, float scale, float zp, float maxq, bool finite) {
+  float q = rintf(__fdiv_rn(x, scale)) + zp;
+  if (finite) return static_cast<uint32_t>(fminf(fmaxf(q, 0.0f), maxq));
+  q = tmin(tmax(q, 0.0f), maxq);
+  return to_code(q);
+}
+
+__global__ void __launch_bounds__(kFastThreads)
+quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
+  constexpr int D = 128, G = 128, G4 = 32;
+  __shared__ __align__(16) uint32_t s_red[8][64][2];   // per warp, per channel pair: (min, max) half2
+  __shared__ float s_scale[D], s_zp[D], s_maxq[D];
+  __shared__ int s_row[D];
+  __shared__ int s_finite[D];
+  __shared__ __align__(16) uint8_t s_low[D * G4];
+  __shared__ __align__(16) uint32_t s_high[128 * G4 / 4];
+  const int K = a.d_boost;
+  const int job = blockIdx.x / a.num_heads;
+  const int h = blockIdx.x - job * a.num_heads;
+  const int tid = threadIdx.x, tg = tid >> 4, cg = tid & 15, warp = tid >> 5, lane = tid & 31;
+  const uint16_t* src = reinterpret_cast<const uint16_t*>(a.key) + a.key_off[job] + h * a.key_s_head;
+  const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
+  const int64_t page = a.dst_page[job];
+
+  Tile8x8 t;
+  load_tile(t, src, a.key_s_tok, tg, cg, G);
+  for (int i = tid; i < K * G4 / 4; i += kFastThreads) s_high[i] = 0u;
+
+  // per channel-pair min / max over this thread's 8 tokens
+  __half2 mn[4], mx[4];
+#pragma unroll
+  for (int w = 0; w < 4; ++w) mn[w] = mx[w] = u2h2(word_of(t.row[0], w));
+#pragma unroll
+  for (int i = 1; i < 8; ++i)
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const __half2 v = u2h2(word_of(t.row[i], w));
+      mn[w] = __hmin2_nan(mn[w], v);
+      mx[w] = __hmax2_nan(mx[w], v);
+    }
+  // lanes l and l^16 hold the other token group of the same channels
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    mn[w] = __hmin2_nan(mn[w], u2h2(__shfl_xor_sync(0xffffffffu, h22u(mn[w]), 16)));
+    mx[w] = __hmax2_nan(mx[w], u2h2(__shfl_xor_sync(0xffffffffu, h22u(mx[w]), 16)));
+  }
+  if (lane < 16) {
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      s_red[warp][4 * cg + w][0] = h22u(mn[w]);
+      s_red[warp][4 * cg + w][1] = h22u(mx[w]);
+    }
+  }
+  __syncthreads();
+  if (tid < 64) {  // channel pair tid: channels 2*tid, 2*tid+1
+    __half2 a2 = u2h2(s_red[0][tid][0]), b2 = u2h2(s_red[0][tid][1]);
+#pragma unroll
+    for (int w = 1; w < 8; ++w) {
+      a2 = __hmin2_nan(a2, u2h2(s_red[w][tid][0]));
+      b2 = __hmax2_nan(b2, u2h2(s_red[w][tid][1]));
+    }
+    uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.key_scale) + page * a.meta_s_page + h * a.meta_s_head;
+    uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.key_zero) + page * a.meta_s_page + h * a.meta_s_head;
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      const int c = 2 * tid + e;
+      const float mnf = e ? __high2float(a2) : __low2float(a2);
+      const float mxf = e ? __high2float(b2) : __low2float(b2);
+      const int r = bidx[c];
+      const bool boosted = r < a.sentinel;
+      const float maxq = boosted ? 15.0f : 3.0f;
+      const float scale = __fdiv_rn(clamp_min(mxf - mnf, 1e-8f), maxq);
+      float zp = rintf(__fdiv_rn(-mnf, scale));
+      zp = tmin(tmax(zp, 0.0f), maxq);
+      s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq;
+      s_row[c] = (boosted && r < K) ? r : -1;
+      s_finite[c] = isfinite(mnf) && isfinite(mxf) && isfinite(scale);
+      out_scale[c] = f2h(scale);
+      out_zero[c] = f2h(zp);
+    }
+  }
+  __syncthreads();
+
+  // quantise: channel c = 8*cg + k, bytes (c, 2*tg) and (c, 2*tg+1)
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int c = 8 * cg + k;
+    const float scale = s_scale[c], zp = s_zp[c], maxq = s_maxq[c];
+    const bool finite = s_finite[c] != 0;
+    uint32_t low = 0u, high = 0u;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint32_t w = word_of(t.row[i], k >> 1);
+      const uint16_t hb = (k & 1) ? uint16_t(w >> 16) : uint16_t(w & 0xffffu);
+      const uint32_t code = quant_code(h2f(hb), scale, zp, maxq, finite);
+      low |= (code & 3u) << (2 * i);
+      high |= ((code >> 2) & 3u) << (2 * i);
+    }
+    *reinterpret_cast<uint16_t*>(s_low + c * G4 + 2 * tg) = uint16_t(low);
+    const int r = s_row[c];
+    if (r >= 0 && high != 0u) {
+      const int byte = r * G4 + 2 * tg;   // 2-byte aligned: never straddles a word
+      atomicOr(&s_high[byte >> 2], high << (8 * (byte & 3)));
+    }
+  }
+  __syncthreads();
+  uint8_t* out_low = a.key_low + page * a.low_s_page + h * a.low_s_head;
+  reinterpret_cast<uint4*>(out_low)[tid] = reinterpret_cast<const uint4*>(s_low)[tid];
+  uint8_t* out_high = a.key_high + page * a.high_s_page + h * a.high_s_head;
+  for (int i = tid; i < K * G4 / 16; i += kFastThreads)
+    reinterpret_cast<uint4*>(out_high)[i] = reinterpret_cast<const uint4*>(s_high)[i];
+}
+
+__global__ void __launch_bounds__(kFastThreads)
+quantize_value_d128_kernel(const KittyValueQuantArgs a) {
+  constexpr int D4 = 32;
+  __shared__ __align__(16) uint8_t s_codes[128 * D4];
+  const int job = blockIdx.x / a.num_heads;
+  const int h = blockIdx.x - job * a.num_heads;
+  const int tid = threadIdx.x, tg = tid >> 4, cg = tid & 15;
+  const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) + a.value_off[job] + h * a.val_s_head;
+  const int n_valid = a.n_valid ? a.n_valid[job] : 128;
+  const int64_t page = a.dst_page[job];
+  Tile8x8 t;
+  load_tile(t, src, a.val_s_tok, tg, cg, n_valid);
+  uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.val_scale) + page * a.meta_s_page + h * a.meta_s_head;
+  uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.val_zero) + page * a.meta_s_page + h * a.meta_s_head;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int tok = 8 * tg + i;
+    // (min, -max) over this thread's 8 channels, then over the 16 lanes of the token row
+    __half2 lo = __hmin2_nan(u2h2(t.row[i].x), u2h2(t.row[i].y));
+    __half2 hi = __hmax2_nan(u2h2(t.row[i].x), u2h2(t.row[i].y));
+    lo = __hmin2_nan(lo, __hmin2_nan(u2h2(t.row[i].z), u2h2(t.row[i].w)));
+    hi = __hmax2_nan(hi, __hmax2_nan(u2h2(t.row[i].z), u2h2(t.row[i].w)));
+    __half2 mm = __halves2half2(__hmin_nan(__low2half(lo), __high2half(lo)),
+                                __hneg(__hmax_nan(__low2half(hi), __high2half(hi))));
+#pragma unroll
+    for (int o = 1; o < 16; o <<= 1) mm = __hmin2_nan(mm, u2h2(__shfl_xor_sync(0xffffffffu, h22u(mm), o)));
+    const float mnf = __low2float(mm), mxf = -__high2float(mm);
+    const float scale = __fdiv_rn(clamp_min(mxf - mnf, 1e-8f), 3.0f);
+    float zp = rintf(__fdiv_rn(-mnf, scale));
+    zp = tmin(tmax(zp, 0.0f), 3.0f);
+    const bool finite = isfinite(mnf) && isfinite(mxf) && isfinite(scale);
+    if (cg == 0) {
+      out_scale[tok * a.meta_s_tok] = f2h(scale);
+      out_zero[tok * a.meta_s_tok] = f2h(zp);
+    }
+    uint32_t bits = 0u;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      const uint32_t w = word_of(t.row[i], k >> 1);
+      const uint16_t hb = (k & 1) ? uint16_t(w >> 16) : uint16_t(w & 0xffffu);
+      bits |= (quant_code(h2f(hb), scale, zp, 3.0f, finite) & 3u) << (2 * k);
+    }
+    *reinterpret_cast<uint16_t*>(s_codes + tok * D4 + 2 * cg) = uint16_t(bits);
+  }
+  __syncthreads();
+  uint8_t* out = a.val_codes + page * a.codes_s_page + h * a.codes_s_head;
+  reinterpret_cast<uint4*>(out)[tid] = reinterpret_cast<const uint4*>(s_codes)[tid];
+}
+
+bool fast_source_ok(const void* base, const int64_t s_tok, const int64_t s_ch) {
+  return s_ch == 1 && (s_tok % 8) == 0 && aligned(base, 16);
+}
+
 size_t key_smem_bytes(int D, int G, int K) {
   return ((size_t(G) * D * 2 + 15) & ~size_t(15)) + size_t(D) * 16 + ((size_t(K) * (G / 4) + 3) / 4) * 4;
 }
@@ -251,6 +463,15 @@ int quantize_key_pages_impl(const KittyKeyQuantArgs* a, void* stream) {
     return fail(KITTY_ERR_UNSUPPORTED, "quantize_key_pages: head_dim*group too large for one CTA");
   if (int64_t(a->n_jobs) * a->num_heads > 0x7fffffffLL)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_key_pages: too many page-heads");
+  // fast path: D = G = 128, token-major 16-byte aligned rows, 16-byte aligned pool slices
+  // (offsets are element offsets: the kernel adds key_off[j]; callers pass multiples of 8)
+  if (a->head_dim == 128 && a->group == 128 && a->d_boost <= 128 &&
+      fast_source_ok(a->key, a->key_s_tok, a->key_s_ch) && (a->key_s_head % 8) == 0 &&
+      aligned(a->key_low, 16) && (a->low_s_page % 16) == 0 && (a->low_s_head % 16) == 0 &&
+      (a->d_boost == 0 || (aligned(a->key_high, 16) && (a->high_s_page % 16) == 0 && (a->high_s_head % 16) == 0))) {
+    quantize_key_d128_kernel<<<a->n_jobs * a->num_heads, kFastThreads, 0, as_stream(stream)>>>(*a);
+    return check_launch("quantize_key_d128_kernel");
+  }
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(quantize_key_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   }
@@ -272,6 +493,12 @@ int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream) {
     return fail(KITTY_ERR_UNSUPPORTED, "quantize_value_pages: head_dim*group too large for one CTA");
   if (int64_t(a->n_jobs) * a->num_heads > 0x7fffffffLL)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_value_pages: too many page-heads");
+  if (a->head_dim == 128 && a->group == 128 && fast_source_ok(a->value, a->val_s_tok, a->val_s_ch) &&
+      (a->val_s_head % 8) == 0 && aligned(a->val_codes, 16) && (a->codes_s_page % 16) == 0 &&
+      (a->codes_s_head % 16) == 0) {
+    quantize_value_d128_kernel<<<a->n_jobs * a->num_heads, kFastThreads, 0, as_stream(stream)>>>(*a);
+    return check_launch("quantize_value_d128_kernel");
+  }
   if (smem > 48 * 1024) {
     cudaFuncSetAttribute(quantize_value_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
   }

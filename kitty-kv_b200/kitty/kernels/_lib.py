@@ -81,6 +81,7 @@ SIGNATURES = {
     "kitty_paged_decode_workspace_size": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(c_size),
                                                          ctypes.POINTER(c_i32)]),
     "kitty_paged_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
+    "kitty_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
 }
 STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs}
 
@@ -123,6 +124,13 @@ def check(rc: int, what: str) -> None:
     if rc != KITTY_OK:
         msg = load().kitty_last_error().decode(errors="replace")
         raise RuntimeError(f"{what} failed ({ERROR_NAMES.get(rc, rc)}): {msg}")
+
+
+def device_error_flags(clear: bool = True) -> int:
+    """Sticky device-side error bits (bit 0: a decode wait timed out); synchronises."""
+    v = ctypes.c_uint32(0)
+    check(load().kitty_device_error_flags(ctypes.byref(v), int(clear)), "kitty_device_error_flags")
+    return v.value
 
 
 def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:
