@@ -73,49 +73,61 @@ def algorithmic_bytes(batch, Hq, H, D, G, K, n_pages, sink, tail):
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and throttle reasons through NVML every 5 ms while the timed
+    region runs (a decode step is well under a millisecond, so nvidia-smi's 200 ms
+    polling would see nothing)."""
+
+    REASONS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+               "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
     def __init__(self, gpu_index: int):
         self.idx = gpu_index
-        self.proc = None
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self.error = None
 
     def __enter__(self):
+        import threading
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", "-i", str(self.idx), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml
+            pynvml.nvmlInit()
+            visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+            phys = int(visible.split(",")[self.idx]) if visible and visible.split(",")[0].isdigit() else self.idx
+            h = pynvml.nvmlDeviceGetHandleByIndex(phys)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # NVML unavailable: report it instead of clocks
+            self.error = f"nvml unavailable: {e}"
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                try:
+                    self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                         pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)))
+                except Exception:
+                    pass
+                time.sleep(0.005)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
+        time.sleep(0.02)
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                self.out, _ = self.proc.communicate()
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
         return False
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = [r.split(", ") for r in self.out.strip().splitlines() if r.strip()]
-        sm = [float(r[1]) for r in rows if len(r) >= 9 and r[1].replace(".", "").isdigit()]
-        mx = [float(r[2]) for r in rows if len(r) >= 9 and r[2].replace(".", "").isdigit()]
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = set()
-        for r in rows:
-            if len(r) >= 9:
-                for n, v in zip(names, r[5:9]):
-                    if v.strip().lower() == "active":
-                        reasons.add(n)
-        loaded = sorted(sm)[len(sm) // 2:] if sm else []
-        return {"sm_mhz": statistics.median(loaded) if loaded else None,
-                "sm_max_mhz": max(mx) if mx else None, "reasons": sorted(reasons), "samples": len(sm)}
+        if self.error:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [self.error], "samples": 0}
+        sm = [c for c, _ in self.samples]
+        reasons = sorted({n for _, r in self.samples for n, bit in self.REASONS.items() if r & bit})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(sm)}
 
 
 # ---------------------------------------------------------------------------
