@@ -199,6 +199,18 @@ int kitty_paged_decode_workspace_size(const KittyDecodeArgs* args, size_t* bytes
 
 int kitty_paged_decode(const KittyDecodeArgs* args, void* stream);
 
+/* Paged decode for callers that cannot allocate device memory (an engine whose
+ * memory arena forbids allocation on the decode path, or a thin FFI host with
+ * no device allocator).  No counterpart in the reference: it runs the same
+ * kernels as kitty_paged_decode but ignores args->workspace and keeps the
+ * split partial results in a static 8 MiB device array inside the library
+ * (held on every GPU that loads the library until exit).  The first call on a
+ * device looks the array up (make it before any stream capture); all calls
+ * share it, so calls that overlap on the GPU race.  With num_splits == 0 the
+ * split count is lowered until the partials fit; an explicit num_splits that
+ * does not fit returns KITTY_ERR_WORKSPACE.  Allocates nothing. */
+int kitty_paged_decode_noalloc(const KittyDecodeArgs* args, void* stream);
+
 /* Sticky error bits set by device code on the current device (bit 0: a decode
  * kernel gave up waiting for a bulk copy after its bounded wait and returned
  * without a valid result).  Synchronises with the device; clear != 0 resets the

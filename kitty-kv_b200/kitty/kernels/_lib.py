@@ -82,6 +82,7 @@ SIGNATURES = {
                                                          ctypes.POINTER(c_i32)]),
     "kitty_paged_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
     "kitty_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
+    "kitty_paged_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
 }
 STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs}
 
