@@ -52,9 +52,16 @@ int validate_decode(const KittyDecodeArgs* a) {
   return KITTY_OK;
 }
 
-// Fill plan.num_splits / pages_per_split / variant (no workspace pointers).
+// Fill plan.num_splits / pages_per_split / variant / grid (no workspace pointers).
 void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
   plan->variant = mma_supports(*a) ? 1 : 0;
+  plan->grid = 0;
+  plan->ws_m = plan->ws_l = plan->ws_o = nullptr;
+  plan->ws_count = nullptr;
+  if (plan->variant == 1) {
+    mma_plan(*a, device_sm_count(), plan);
+    return;
+  }
   const int maxp = std::max(0, a->max_pages_per_seq);
   const int64_t units = int64_t(a->batch) * a->num_kv_heads;
   int splits;
@@ -73,11 +80,12 @@ void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
 }
 
 size_t workspace_bytes(const KittyDecodeArgs* a, const DecodePlan& plan) {
-  if (plan.num_splits <= 1) return 0;
+  if (plan.variant == 0 && plan.num_splits <= 1) return 0;
   const size_t g = size_t(a->num_q_heads / a->num_kv_heads);
   const size_t n = size_t(a->batch) * a->num_kv_heads * plan.num_splits * g;
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-  return up(n * 4) * 2 + up(n * a->head_dim * 4);
+  const size_t counts = plan.variant == 1 ? up(size_t(a->batch) * a->num_kv_heads * 4) : 0;
+  return up(n * 4) * 2 + up(n * a->head_dim * 4) + counts;
 }
 
 }  // namespace
@@ -160,11 +168,12 @@ int kitty_paged_decode(const KittyDecodeArgs* args, void* stream) {
     plan.ws_m = reinterpret_cast<float*>(w);
     plan.ws_l = reinterpret_cast<float*>(w + up(n * 4));
     plan.ws_o = reinterpret_cast<float*>(w + 2 * up(n * 4));
+    if (plan.variant == 1) plan.ws_count = reinterpret_cast<int*>(w + 2 * up(n * 4) + up(n * args->head_dim * 4));
   }
   cudaStream_t s = as_stream(stream);
   rc = plan.variant == 1 ? launch_decode_mma(*args, plan, s) : launch_decode_simt(*args, plan, s);
   if (rc != KITTY_OK) return rc;
-  if (plan.num_splits > 1) rc = launch_decode_merge(*args, plan, s);
+  if (plan.variant == 1 || plan.num_splits > 1) rc = launch_decode_merge(*args, plan, s);
   return rc;
 }
 

@@ -9,13 +9,22 @@ namespace kitty {
 // sequence covers its pages [s*pages_per_split, (s+1)*pages_per_split); split 0
 // also covers the fp16 sinks and tail.  With num_splits == 1 the decode kernel
 // writes the final output itself and no workspace is used.
+//
+// The tensor-core variant uses the fields differently: every warp walks a
+// contiguous slice of the (sequence, KV head, item) space and writes one
+// partial per (sequence, KV head) it touches; num_splits is then the number of
+// partial slots per (sequence, KV head), pages_per_split the minimum slice
+// length, grid the persistent grid size, and ws_count[b][h] receives the number
+// of slots written.
 struct DecodePlan {
   int num_splits;
   int pages_per_split;
   int variant;        // 0 = CUDA-core (any shape), 1 = tensor-core (D = G = 128)
-  float* ws_m;        // [B][H][S][g] running max per split
+  int grid;           // tensor-core variant: CTAs of the persistent grid
+  float* ws_m;        // [B][H][S][g] running max per split (natural log units)
   float* ws_l;        // [B][H][S][g] running sum per split
   float* ws_o;        // [B][H][S][g][D] unnormalised accumulator per split
+  int* ws_count;      // [B][H] slots written (tensor-core variant), else nullptr
 };
 
 int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
@@ -24,6 +33,7 @@ int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaSt
 bool simt_supports(const KittyDecodeArgs& a);
 bool mma_supports(const KittyDecodeArgs& a);
 int mma_ctas_per_sm();
+void mma_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
 int read_decode_error(uint32_t* flags, int clear);
 
 }  // namespace kitty

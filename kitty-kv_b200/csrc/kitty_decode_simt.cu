@@ -263,17 +263,19 @@ __global__ void decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   const int H = a.num_kv_heads, g = a.num_q_heads / H, D = a.head_dim;
   const int h = qhg / g, qh = qhg - h * g;
   const int64_t base = (int64_t(b) * H + h) * plan.num_splits;
+  // slots written for this (sequence, head): all of them, or the recorded count
+  const int nsl = plan.ws_count ? min(max(plan.ws_count[int64_t(b) * H + h], 0), plan.num_splits) : plan.num_splits;
   float M = -INFINITY;
-  for (int s = 0; s < plan.num_splits; ++s) M = fmaxf(M, plan.ws_m[(base + s) * g + qh]);
+  for (int s = 0; s < nsl; ++s) M = fmaxf(M, plan.ws_m[(base + s) * g + qh]);
   float L = 0.f;
-  for (int s = 0; s < plan.num_splits; ++s) {
+  for (int s = 0; s < nsl; ++s) {
     const float m = plan.ws_m[(base + s) * g + qh];
     if (m != -INFINITY) L += __expf(m - M) * plan.ws_l[(base + s) * g + qh];
   }
   uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + qhg * a.out_s_head;
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
     float acc = 0.f;
-    for (int s = 0; s < plan.num_splits; ++s) {
+    for (int s = 0; s < nsl; ++s) {
       const float m = plan.ws_m[(base + s) * g + qh];
       if (m != -INFINITY) acc += __expf(m - M) * plan.ws_o[((base + s) * g + qh) * D + c];
     }

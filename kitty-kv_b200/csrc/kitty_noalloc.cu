@@ -74,12 +74,16 @@ extern "C" int kitty_paged_decode_noalloc(const KittyDecodeArgs* args, void* str
                              std::to_string(need) + " bytes of scratch; the static scratch holds " +
                              std::to_string(kNoAllocScratchBytes) + " (pass num_splits=0 to let it fit)");
     }
-    // fewer splits until the partial results fit (one split needs no scratch at all)
-    while (splits > 1 && need > kNoAllocScratchBytes) {
-      a.num_splits = splits - 1;
+    // lower the requested split count until the partial results fit
+    for (int32_t target = splits - 1; target >= 1 && need > kNoAllocScratchBytes; --target) {
+      a.num_splits = target;
       rc = kitty_paged_decode_workspace_size(&a, &need, &splits);
       if (rc != KITTY_OK) return rc;
     }
+    if (need > kNoAllocScratchBytes)
+      return kitty::fail(KITTY_ERR_WORKSPACE, "paged_decode_noalloc: even one split needs " + std::to_string(need) +
+                                                  " bytes of scratch; the static scratch holds " +
+                                                  std::to_string(kNoAllocScratchBytes));
   }
   void* scratch = nullptr;
   if (need > 0) {

@@ -142,7 +142,9 @@ def test_random_batches_vs_oracle(seed, B, Hq, H, ctx, rate):
 def test_large_context_properties():
     """Benchmark-config-2-like sequence lengths (255 pages): the result does not depend on
     the split count, and permuting the page order together with the physical pages
-    leaves it unchanged (softmax is order invariant) - checked without the oracle."""
+    leaves it unchanged (softmax is order invariant) - checked without the oracle, at the
+    fp16 output tolerance (how the pages are split over warps changes the running max
+    that p * scale_v is rounded against, so the results agree to rounding, not bitwise)."""
     case = synthetic.make_decode_case(7, 2, 32, 8, 128, [32768, 32 + 200 * 128 + 50])
     total = sum(s.n_pages for s in case.seqs)
     phys_of = GC.phys_layout(case, 7, total + 1)
@@ -150,7 +152,7 @@ def test_large_context_properties():
     base = run_batched(case, pools, phys_of, num_splits=1)
     assert np.isfinite(base).all()
     for splits in (0, 2, 17, 255):
-        assert_close(run_batched(case, pools, phys_of, num_splits=splits), base, atol=5e-4, rtol=5e-3)
+        assert_close(run_batched(case, pools, phys_of, num_splits=splits), base)
     # reversed logical order of pages: same set of (key, value) tokens -> same output
     sk, sv, sl, tk, tv, tl = GC.padded_regions(case)
     bt, npg = GC.block_table(case, phys_of)
@@ -161,4 +163,4 @@ def test_large_context_properties():
                                      case.d_boost, sink_k=cuda(sk), sink_v=cuda(sv), sink_len=cuda(sl),
                                      tail_k=cuda(tk), tail_v=cuda(tv), tail_len=cuda(tl))
     torch.cuda.synchronize()
-    assert_close(out.cpu().numpy(), base, atol=5e-4, rtol=5e-3)
+    assert_close(out.cpu().numpy(), base)

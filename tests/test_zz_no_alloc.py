@@ -114,8 +114,8 @@ def test_noalloc_rejects_explicit_splits_beyond_the_scratch():
     q = torch.zeros(3, 32, 128, dtype=torch.float16, device=DEV)
     out = torch.empty_like(q)
     a = _args(case, pools, bidx, bt, npg, sk, sv, tk, tv, tl, q, out)
-    # batch 3 x 32 heads x 130 floats = 49920 B per split: 256 splits exceed 8 MiB
-    a.num_splits = 256
-    a.max_pages_per_seq = 256
+    # partials for ~2^19 splits of 3 x 32 query heads x 130 floats are far beyond 8 MiB
+    a.num_splits = 1 << 20
+    a.max_pages_per_seq = 1 << 20
     rc = lib.kitty_paged_decode_noalloc(a, stream)
     assert rc == 4 and b"static scratch" in lib.kitty_last_error()
