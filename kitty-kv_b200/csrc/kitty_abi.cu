@@ -1,5 +1,6 @@
 // C ABI entry points: argument validation, split planning, dispatch.
 #include <algorithm>
+#include <atomic>
 #include <cstring>
 #include <mutex>
 
@@ -13,6 +14,7 @@ int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream);
 
 namespace {
 thread_local std::string g_last_error;
+std::atomic<int> g_forced_variant{-1};   // -1: the library chooses
 
 int device_sm_count() {
   int dev = 0;
@@ -53,11 +55,25 @@ int validate_decode(const KittyDecodeArgs* a) {
 }
 
 // Fill plan.num_splits / pages_per_split / variant / grid (no workspace pointers).
+int choose_variant(const KittyDecodeArgs* a) {
+  const int forced = g_forced_variant.load();
+  if (forced == 2 && i8_supports(*a)) return 2;
+  if (forced == 1 && mma_supports(*a)) return 1;
+  if (forced == 0) return 0;
+  if (i8_supports(*a)) return 2;
+  if (mma_supports(*a)) return 1;
+  return 0;
+}
+
 void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
-  plan->variant = mma_supports(*a) ? 1 : 0;
+  plan->variant = choose_variant(a);
   plan->grid = 0;
   plan->ws_m = plan->ws_l = plan->ws_o = nullptr;
   plan->ws_count = nullptr;
+  if (plan->variant == 2) {
+    i8_plan(*a, device_sm_count(), plan);
+    return;
+  }
   if (plan->variant == 1) {
     mma_plan(*a, device_sm_count(), plan);
     return;
@@ -84,7 +100,7 @@ size_t workspace_bytes(const KittyDecodeArgs* a, const DecodePlan& plan) {
   const size_t g = size_t(a->num_q_heads / a->num_kv_heads);
   const size_t n = size_t(a->batch) * a->num_kv_heads * plan.num_splits * g;
   auto up = [](size_t x) { return (x + 255) & ~size_t(255); };
-  const size_t counts = plan.variant == 1 ? up(size_t(a->batch) * a->num_kv_heads * 4) : 0;
+  const size_t counts = plan.variant >= 1 ? up(size_t(a->batch) * a->num_kv_heads * 4) : 0;
   return up(n * 4) * 2 + up(n * a->head_dim * 4) + counts;
 }
 
@@ -132,7 +148,22 @@ int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream) {
 int kitty_device_error_flags(uint32_t* flags, int clear) {
   clear_error();
   if (!flags) return fail(KITTY_ERR_INVALID_ARGUMENT, "device_error_flags: flags is NULL");
-  return read_decode_error(flags, clear);
+  uint32_t a = 0, b = 0;
+  int rc = read_decode_error(&a, clear);
+  if (rc != KITTY_OK) return rc;
+  rc = read_decode_error_i8(&b, clear);
+  if (rc != KITTY_OK) return rc;
+  *flags = a | b;
+  return KITTY_OK;
+}
+
+int kitty_decode_force_variant(int variant, int* previous) {
+  clear_error();
+  if (variant < -1 || variant > 2)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "decode_force_variant: variant must be -1, 0, 1 or 2");
+  const int old = g_forced_variant.exchange(variant);
+  if (previous) *previous = old;
+  return KITTY_OK;
 }
 
 int kitty_paged_decode_workspace_size(const KittyDecodeArgs* args, size_t* bytes, int32_t* num_splits_out) {
@@ -168,12 +199,14 @@ int kitty_paged_decode(const KittyDecodeArgs* args, void* stream) {
     plan.ws_m = reinterpret_cast<float*>(w);
     plan.ws_l = reinterpret_cast<float*>(w + up(n * 4));
     plan.ws_o = reinterpret_cast<float*>(w + 2 * up(n * 4));
-    if (plan.variant == 1) plan.ws_count = reinterpret_cast<int*>(w + 2 * up(n * 4) + up(n * args->head_dim * 4));
+    if (plan.variant >= 1) plan.ws_count = reinterpret_cast<int*>(w + 2 * up(n * 4) + up(n * args->head_dim * 4));
   }
   cudaStream_t s = as_stream(stream);
-  rc = plan.variant == 1 ? launch_decode_mma(*args, plan, s) : launch_decode_simt(*args, plan, s);
+  rc = plan.variant == 2   ? launch_decode_i8(*args, plan, s)
+       : plan.variant == 1 ? launch_decode_mma(*args, plan, s)
+                           : launch_decode_simt(*args, plan, s);
   if (rc != KITTY_OK) return rc;
-  if (plan.variant == 1 || plan.num_splits > 1) rc = launch_decode_merge(*args, plan, s);
+  if (plan.variant >= 1 || plan.num_splits > 1) rc = launch_decode_merge(*args, plan, s);
   return rc;
 }
 

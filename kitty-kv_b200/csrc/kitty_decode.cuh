@@ -10,7 +10,7 @@ namespace kitty {
 // also covers the fp16 sinks and tail.  With num_splits == 1 the decode kernel
 // writes the final output itself and no workspace is used.
 //
-// The tensor-core variant uses the fields differently: every warp walks a
+// The tensor-core variants use the fields differently: every warp walks a
 // contiguous slice of the (sequence, KV head, item) space and writes one
 // partial per (sequence, KV head) it touches; num_splits is then the number of
 // partial slots per (sequence, KV head), pages_per_split the minimum slice
@@ -19,7 +19,8 @@ namespace kitty {
 struct DecodePlan {
   int num_splits;
   int pages_per_split;
-  int variant;        // 0 = CUDA-core (any shape), 1 = tensor-core (D = G = 128)
+  int variant;        // 0 = CUDA-core (any shape), 1 = fp16 tensor-core (D = G = 128, g <= 8),
+                      // 2 = integer tensor-core (D = G = 128, g <= 4)
   int grid;           // tensor-core variant: CTAs of the persistent grid
   float* ws_m;        // [B][H][S][g] running max per split (natural log units)
   float* ws_l;        // [B][H][S][g] running sum per split
@@ -35,5 +36,10 @@ bool mma_supports(const KittyDecodeArgs& a);
 int mma_ctas_per_sm();
 void mma_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
 int read_decode_error(uint32_t* flags, int clear);
+int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
+bool i8_supports(const KittyDecodeArgs& a);
+int i8_ctas_per_sm();
+void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
+int read_decode_error_i8(uint32_t* flags, int clear);
 
 }  // namespace kitty

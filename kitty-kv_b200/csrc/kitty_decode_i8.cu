@@ -1,0 +1,756 @@
+// Paged GQA decode attention with integer tensor-core contractions
+// (head_dim = group = 128, up to 4 query heads per KV head).
+//
+// Work decomposition and data movement are those of the fp16 tensor-core
+// kernel (kitty_decode_mma.cu): segments (sequence, KV head) of items (item 0 =
+// fp16 sinks + tail, items 1..n = quantised pages), one contiguous slice of
+// items per warp, one partial result per touched segment, per-warp key and
+// value buffers filled by 1-D bulk async copies on bounded mbarrier waits.
+//
+// What changes is the arithmetic of a page-head.  The 2-bit codes stay
+// integers: one AND per register extracts four codes into the bytes of an
+// 8-bit MMA operand (mma.sync.m16n8k32, u8 x u8 -> s32), and the other operand
+// carries the folded scales in fixed point:
+//
+//   keys    w[qh][c] = q[qh][c] * scale_k[c]           (exact in fp32)
+//           x[qh][c] = rint(w * R),  R = (2^22 - 4) / max_c |w|
+//           x is split into bytes: x = 65536 (b2 - 64) + 256 b1 + b0 (b0, b1, b2
+//           unsigned), so  sum_c code * x = 65536 (S[b2] - 64 S[1]) + 256 S[b1] + S[b0]
+//           where S[d] is the MMA sum against digit plane d and S[1] the code sum
+//           (an all-ones plane).  Scores = (sum_c code * x) / R - sum_c zp_k w,
+//           i.e. 23 significant bits per product (16 bits moved the logits by up
+//           to ~1e-3, too much next to the value outliers).
+//   values  P'[qh][t] = p[qh][t] * scale_v[t]           (fp32)
+//           y[qh][t] = rint(P' * Rv), Rv = 65535 / max_t P'   (two unsigned digits)
+//           O[c][qh] += (sum_t code_v * y - sum_t zp_v * y) / Rv
+//           (the zero-point sum uses the same rounded y, so (code - zp) is
+//           weighted consistently).
+//
+// Per MMA the 8 columns are 4 query heads x 2 digits (hi, lo), so one lane holds
+// both digits of the same (token, query head) and combines them with one
+// integer multiply-add: no exchange between lanes, and after the key
+// contraction lane (g_, q_) owns the 16 scores of query head q_ for the tokens
+// 16 g_ .. 16 g_ + 15 (the same 16 channels of the value accumulator).
+//
+// Operand layout.  A 4x4 byte transpose (8 byte permutes) turns word g_ of four
+// rows into four words, each holding byte j of the four rows; masking bit pair
+// i of every byte gives the A operand of code 4 j + i of four rows, scaled by
+// 4^i.  The scale is removed per output row in the fp32 epilogue.  Keys use
+// the factors (1, 4, 16, 16) for i = 0..3 (i = 3 shifted down by two bits) so
+// that the boosted high plane can reuse the same accumulators with its
+// factor 4 built into the masks ((4, 16, 64, 64) * high code).  The K index
+// (channels for keys, tokens for values) is permuted so that the 32 lanes'
+// word loads of a k-step hit 32 distinct banks; the fixed-point digit tables
+// are stored in the same permuted order.
+//
+// Reference semantics: (code - zp) * scale from kitty/kernels/dequantize_key.py:89-95
+// and kitty/kernels/quantize_value.py:121-133; softmax over [sinks ; pages ;
+// tail] as in kitty/kernels/attention.py:172-189.
+
+#include <algorithm>
+
+#include "kitty_decode.cuh"
+#include "kitty_ptx.cuh"
+
+namespace kitty {
+
+__device__ unsigned int g_decode_error_i8 = 0;  // bit 0: a bulk-copy wait timed out
+
+namespace {
+
+using namespace dev;
+
+constexpr int kWarps = 4;
+constexpr int kThreads = kWarps * 32;
+constexpr int kCtasPerSm = 3;
+constexpr int kD = 128, kG = 128;
+constexpr float kLog2e = 1.4426950408889634f;
+constexpr float kLn2 = 0.6931471805599453f;
+constexpr int kSlotsTarget = 16;
+constexpr float kKeyRange = 4194300.0f;     // 2^22 - 4: |x| < 2^22 even with an approximate reciprocal
+constexpr float kValRange = 65535.0f;
+constexpr float kMagicKey = 12582912.0f;    // 1.5 * 2^23: fma(w, R, magic) has bits 0x4B400000 + rint(w R)
+constexpr float kMagicVal = 8388608.0f;     // 2^23: fma(P', Rv, magic) has bits 0x4B000000 + rint(P' Rv)
+constexpr int kPlane = 576;                 // digit table: plane stride (bytes)
+constexpr int kRow = 144;                   // digit table: query-head row stride (bytes)
+constexpr int kPhRow = 136;                 // fp16 P staging (fp16 region): row stride in halves
+
+// per-warp shared memory (bytes)
+struct Layout {
+  int kbuf, vbuf, dtab, ptab, ent, bars, size;
+};
+__host__ __device__ inline Layout i8_layout(int K) {
+  Layout L;
+  int o = 0;
+  L.kbuf = o; o += (4096 + 512 + K * 32 + 32 + 127) & ~127;  // low plane, scale/zero rows, high plane, zero row
+  L.vbuf = o; o += 4096 + 512;                               // codes, (scale, zero) per token
+  L.dtab = o; o += 4 * kPlane;                               // key digits b0, b1, b2, ones [qh][channel]
+  L.ptab = o; o += 2 * kPlane;                               // P' digits y0, y1 [qh][token] / fp16 P (fp16 region)
+  L.ent = o;  o += 128 * 4;                                  // boosted entries (row offset | position << 16)
+  L.bars = o; o += 16;
+  L.size = (o + 127) & ~127;
+  return L;
+}
+
+// ---- integer MMA and operand helpers -----------------------------------------
+
+__device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
+__device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                        uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+// exact product of two fp16 values in fp32
+__device__ __forceinline__ float mul_f16_f32(uint16_t a, uint16_t b) {
+  float d;
+  asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(0.0f));
+  return d;
+}
+// 4x4 byte transpose: t[j] byte r = byte j of u[r]
+__device__ __forceinline__ void transpose4(const uint32_t (&u)[4], uint32_t (&t)[4]) {
+  const uint32_t a = prmt(u[0], u[1], 0x5140u), b = prmt(u[0], u[1], 0x7362u);
+  const uint32_t c = prmt(u[2], u[3], 0x5140u), d = prmt(u[2], u[3], 0x7362u);
+  t[0] = prmt(a, c, 0x5410u);
+  t[1] = prmt(a, c, 0x7632u);
+  t[2] = prmt(b, d, 0x5410u);
+  t[3] = prmt(b, d, 0x7632u);
+}
+// code i of every byte of t, times the row factor (see the header comment)
+template <int i>
+__device__ __forceinline__ uint32_t key_code(uint32_t t) {
+  return i < 3 ? (t & (0x03030303u << (2 * i))) : ((t >> 2) & 0x30303030u);
+}
+template <int i>
+__device__ __forceinline__ uint32_t high_code(uint32_t t) {   // 4 * key_code factor
+  return i < 3 ? ((t << 2) & (0x0C0C0C0Cu << (2 * i))) : (t & 0xC0C0C0C0u);
+}
+template <int i>
+__device__ __forceinline__ uint32_t val_code(uint32_t t) {
+  return t & (0x03030303u << (2 * i));
+}
+// bytes k of v0..v3 packed into one word
+__device__ __forceinline__ void bytes01(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t& w0,
+                                        uint32_t& w1) {
+  const uint32_t a = prmt(v0, v1, 0x5140u), b = prmt(v2, v3, 0x5140u);
+  w0 = prmt(a, b, 0x5410u);
+  w1 = prmt(a, b, 0x7632u);
+}
+__device__ __forceinline__ uint32_t byte2(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
+  return prmt(prmt(v0, v1, 0x0062u), prmt(v2, v3, 0x0062u), 0x5410u);
+}
+// permuted K position of channel / token c (see the header comment)
+__device__ __forceinline__ int kpos(int c) { return (c & ~15) | ((c & 3) << 2) | ((c >> 2) & 3); }
+
+struct State {
+  float o[16];   // unnormalised accumulator, channels 16 g_ + v, query head q_
+  float m;       // running max (log2 domain)
+  float l;       // running sum over this lane's tokens
+  float zs;      // value zero-point sums over this lane's tokens (already divided by Rv)
+};
+
+__device__ __forceinline__ void reset_state(State& st) {
+#pragma unroll
+  for (int v = 0; v < 16; ++v) st.o[v] = 0.f;
+  st.m = -INFINITY;
+  st.l = 0.f;
+  st.zs = 0.f;
+}
+
+// Online-softmax step over the lane's 16 scores (log2 domain; -inf = masked).
+// Returns p in s.
+__device__ __forceinline__ void softmax_step(State& st, float (&s)[16]) {
+  float mx = s[0];
+#pragma unroll
+  for (int v = 1; v < 16; ++v) mx = fmaxf(mx, s[v]);
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
+  mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
+  const float mn = fmaxf(st.m, mx);
+  const float alpha = (st.m == -INFINITY) ? 0.f : ex2(st.m - mn);
+  // a fully masked chunk before any real token keeps everything at zero
+  const float base = (mn == -INFINITY) ? 0.f : mn;
+  st.m = mn;
+  float sum = 0.f;
+#pragma unroll
+  for (int v = 0; v < 16; ++v) {
+    s[v] = ex2(s[v] - base);
+    sum += s[v];
+  }
+  st.l = st.l * alpha + sum;
+  st.zs *= alpha;
+#pragma unroll
+  for (int v = 0; v < 16; ++v) st.o[v] *= alpha;
+}
+
+// Per-segment setup: q of the prep lane's (query head, 16 channels) and the
+// boosted-entry table.  Returns the number of boosted entries.
+__device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint8_t* wsm, const Layout& L,
+                             int lane, uint32_t (&qreg)[8]) {
+  const int pq = lane >> 3, cb = lane & 7;
+  if (pq < g) {
+    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
+                                                      int64_t(h * g + pq) * a.q_s_head + 16 * cb);
+    const uint4 x0 = src[0], x1 = src[1];
+    qreg[0] = x0.x; qreg[1] = x0.y; qreg[2] = x0.z; qreg[3] = x0.w;
+    qreg[4] = x1.x; qreg[5] = x1.y; qreg[6] = x1.z; qreg[7] = x1.w;
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) qreg[i] = 0u;
+  }
+  uint32_t* ent = reinterpret_cast<uint32_t*>(wsm + L.ent);
+  const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
+  const uint32_t zero_row = uint32_t(a.d_boost) * 32u;
+  int nb = 0;
+  for (int c0 = 0; c0 < kD; c0 += 32) {
+    const int c = c0 + lane;
+    const int r = bidx[c];
+    const bool boosted = r < a.d_boost;
+    const uint32_t bal = __ballot_sync(0xffffffffu, boosted);
+    if (boosted) ent[nb + __popc(bal & ((1u << lane) - 1u))] = uint32_t(r) * 32u | (uint32_t(kpos(c)) << 16);
+    nb += __popc(bal);
+  }
+  // pad to a multiple of 16 entries with the zero row
+  const int padded = (nb + 15) & ~15;
+  if (nb + lane < padded) ent[nb + lane] = zero_row;
+  __syncwarp();
+  return nb;
+}
+
+// fp16 region of (b, h): sinks then tail, 128 tokens per chunk (fp16 MMAs).
+// Token / channel 16 g_ + 2 m + h of the lane <-> row g_ + 8 h of M tile m.
+__device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, State& st, uint8_t* wsm,
+                                    const Layout& L, float qk_scale, int lane) {
+  const int g_ = lane >> 2, q_ = lane & 3;
+  const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
+  const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
+  const int total = sink_len + tail_len;
+  if (total <= 0) return;
+  __half* ph = reinterpret_cast<__half*>(wsm + L.ptab);
+  // q of query head g_ >> 1 (B column g_), channels 32 q_ .. 32 q_ + 31: the K
+  // index (2q_, 2q_+1, 2q_+8, 2q_+9) of k-step s <-> channel 32 q_ + 4 s + (0..3)
+  uint32_t qw[16];
+  {
+    const int qh = g_ >> 1;
+    if (qh < g) {
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
+                                                        int64_t(h * g + qh) * a.q_s_head + 32 * q_);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const uint4 x = src[i];
+        qw[4 * i] = x.x; qw[4 * i + 1] = x.y; qw[4 * i + 2] = x.z; qw[4 * i + 3] = x.w;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) qw[i] = 0u;
+    }
+  }
+  for (int f0 = 0; f0 < total; f0 += kG) {
+    const int ntok = min(kG, total - f0);
+    auto row = [&](bool key, int t) -> const uint16_t* {   // row of chunk token t (t < ntok)
+      const int ft = f0 + t;
+      if (ft < sink_len) {
+        return key ? reinterpret_cast<const uint16_t*>(a.sink_k) + b * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
+                   : reinterpret_cast<const uint16_t*>(a.sink_v) + b * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok;
+      }
+      const int tt = ft - sink_len;
+      return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + b * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
+                 : reinterpret_cast<const uint16_t*>(a.tail_v) + b * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
+    };
+    float s[16];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      float acc[4] = {0.f, 0.f, 0.f, 0.f};
+      const int ta = 16 * g_ + 2 * m, tb = ta + 1;
+      uint4 ka[4], kb[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) { ka[i] = make_uint4(0, 0, 0, 0); kb[i] = ka[i]; }
+      if (ta < ntok) {
+        const uint4* r = reinterpret_cast<const uint4*>(row(true, ta) + 32 * q_);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) ka[i] = r[i];
+      }
+      if (tb < ntok) {
+        const uint4* r = reinterpret_cast<const uint4*>(row(true, tb) + 32 * q_);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) kb[i] = r[i];
+      }
+      const uint32_t* wa = reinterpret_cast<const uint32_t*>(ka);
+      const uint32_t* wb = reinterpret_cast<const uint32_t*>(kb);
+#pragma unroll
+      for (int k = 0; k < 8; ++k) mma_f16(acc, wa[2 * k], wb[2 * k], wa[2 * k + 1], wb[2 * k + 1], qw[2 * k], qw[2 * k + 1]);
+      s[2 * m] = ta < ntok ? acc[0] * qk_scale : -INFINITY;
+      s[2 * m + 1] = tb < ntok ? acc[2] * qk_scale : -INFINITY;
+    }
+    softmax_step(st, s);
+    // P (scale 1) as fp16 [query head q_][token]
+    {
+      uint32_t w[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) w[k] = pack_f32x2(s[2 * k], s[2 * k + 1]);
+      uint4* dst = reinterpret_cast<uint4*>(ph + q_ * kPhRow + 16 * g_);
+      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
+      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+    }
+    __syncwarp();
+    // values: M = channels 16 g_ + 2 m (+1), K = tokens 16 k + (2q_, 2q_+1, 2q_+8, 2q_+9)
+    float oacc[8][4];
+#pragma unroll
+    for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
+    const __half* pb = ph + (g_ >> 1) * kPhRow;
+#pragma unroll 1
+    for (int k = 0; k < 8; ++k) {
+      uint4 v[4][2];
+      const int t0 = 16 * k + 2 * q_;
+      const int ts[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        if (ts[e] < ntok) {
+          const uint4* r = reinterpret_cast<const uint4*>(row(false, ts[e]) + 16 * g_);
+          v[e][0] = r[0]; v[e][1] = r[1];
+        } else {
+          v[e][0] = v[e][1] = make_uint4(0, 0, 0, 0);
+        }
+      }
+      const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + t0);
+      const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + t0 + 8);
+      const uint32_t* w0 = reinterpret_cast<const uint32_t*>(v[0]);
+      const uint32_t* w1 = reinterpret_cast<const uint32_t*>(v[1]);
+      const uint32_t* w2 = reinterpret_cast<const uint32_t*>(v[2]);
+      const uint32_t* w3 = reinterpret_cast<const uint32_t*>(v[3]);
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        mma_f16(oacc[m], prmt(w0[m], w1[m], 0x5410u), prmt(w0[m], w1[m], 0x7632u), prmt(w2[m], w3[m], 0x5410u),
+                prmt(w2[m], w3[m], 0x7632u), b0, b1);
+      }
+    }
+#pragma unroll
+    for (int m = 0; m < 8; ++m) {
+      st.o[2 * m] += oacc[m][0];
+      st.o[2 * m + 1] += oacc[m][2];
+    }
+    __syncwarp();
+  }
+}
+
+__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+  extern __shared__ __align__(128) uint8_t smem[];
+  const int K = a.d_boost, H = a.num_kv_heads, B = a.batch;
+  const int g = a.num_q_heads / H;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g_ = lane >> 2, q_ = lane & 3;
+  const int pq = lane >> 3, cb = lane & 7;
+  const Layout L = i8_layout(K);
+  uint8_t* wsm = smem + warp * L.size;
+  uint8_t* kbuf = wsm + L.kbuf;
+  uint8_t* vbuf = wsm + L.vbuf;
+  uint8_t* dtab = wsm + L.dtab;
+  uint8_t* ptab = wsm + L.ptab;
+  const uint32_t* ent = reinterpret_cast<const uint32_t*>(wsm + L.ent);
+  const uint32_t bar_k = smem_u32(wsm + L.bars), bar_v = bar_k + 8;
+
+  // ---- this warp's slice of the item space
+  const int64_t gw = int64_t(blockIdx.x) * kWarps + warp;
+  const int64_t n_warps = int64_t(gridDim.x) * kWarps;
+  SegmentScan sc = scan_segments(a.num_pages, B, H, 0, lane);
+  const int64_t total = sc.total;
+  int64_t F = (total + n_warps - 1) / n_warps;
+  if (F < plan.pages_per_split) F = plan.pages_per_split;
+  const int64_t f0 = gw * F;
+  if (f0 >= total) return;
+  const int64_t f1 = min(total, f0 + F);
+  sc = scan_segments(a.num_pages, B, H, f0, lane);
+  int b = sc.b, h = sc.h, p = sc.p;
+  int slot = int(gw - sc.seg_begin / F);
+
+  if (lane == 0) {
+    mbar_init(bar_k, 1);
+    mbar_init(bar_v, 1);
+  }
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+  // constant tables: the all-ones digit plane and the zero row after the high plane
+  for (int i = lane; i < kPlane / 4; i += 32) reinterpret_cast<uint32_t*>(dtab + 3 * kPlane)[i] = 0x01010101u;
+  if (lane < 8) reinterpret_cast<uint32_t*>(kbuf + 4608 + K * 32)[lane] = 0u;
+  __syncwarp();
+
+  const float qk_scale = a.sm_scale * kLog2e;
+  const int64_t ph_low = int64_t(kD) * (kG / 4), ph_high = int64_t(K) * (kG / 4);
+  const uint32_t bytes_high = uint32_t(ph_high);
+  const uint32_t k_tx = 4096u + 512u + bytes_high, v_tx = 4096u + 512u;
+  uint32_t k_phase = 0, v_phase = 0;
+  bool failed = false;
+
+  auto phys = [&](int bb, int pp) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - 1)]; };
+  auto issue_k = [&](const Cursor& c) {
+    int64_t page = phys(c.b, c.p);
+    if (page < 0 || page >= a.pool_pages) page = 0;
+    const int64_t phh = page * H + c.h;
+    mbar_arrive_expect_tx(bar_k, k_tx);
+    bulk_g2s(smem_u32(kbuf), a.key_low + phh * ph_low, 4096u, bar_k);
+    bulk_g2s(smem_u32(kbuf + 4096), reinterpret_cast<const uint8_t*>(a.key_meta) + phh * (2 * kD * 2), 512u, bar_k);
+    if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
+  };
+  auto issue_v = [&](const Cursor& c) {
+    int64_t page = phys(c.b, c.p);
+    if (page < 0 || page >= a.pool_pages) page = 0;
+    const int64_t phh = page * H + c.h;
+    mbar_arrive_expect_tx(bar_v, v_tx);
+    bulk_g2s(smem_u32(vbuf), a.val_codes + phh * ph_low, 4096u, bar_v);
+    bulk_g2s(smem_u32(vbuf + 4096), reinterpret_cast<const uint8_t*>(a.val_meta) + phh * (2 * kG * 2), 512u, bar_v);
+  };
+
+  Cursor cur{f0, b, h, p};
+  bool have_next = cursor_to_page(cur, a.num_pages, H, f1);
+  if (lane == 0 && have_next) { issue_k(cur); issue_v(cur); }
+  __syncwarp();
+
+  State st;
+  reset_state(st);
+  uint32_t qreg[8];
+  int nb = setup_segment(a, b, h, g, wsm, L, lane, qreg);
+
+  // B operand bases: column g_ of an MMA = query head g_ >> 1, digit (g_ & 1 ? lo : hi)
+  const uint8_t* kb1 = dtab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;   // b1 | b0
+  const uint8_t* kb2 = dtab + ((g_ & 1) ? 3 : 2) * kPlane + (g_ >> 1) * kRow;   // b2 | ones
+  const uint8_t* vb = ptab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;    // y1 | y0
+
+  for (int64_t f = f0; f < f1; ++f) {
+    if (p == 0) {
+      process_fp16_region(a, b, h, g, st, wsm, L, qk_scale, lane);
+    } else {
+      const int64_t page = phys(b, p);
+      const bool valid = page >= 0 && page < a.pool_pages;
+      if (!mbar_wait(bar_k, k_phase)) { failed = true; break; }
+      k_phase ^= 1u;
+      const uint8_t* km = kbuf + 4096;   // scale[128] fp16, zero[128] fp16
+      const uint8_t* kh = kbuf + 4608;   // high plane rows, then the zero row
+
+      // ---- key digits: prep lane (query head pq, channels 16 cb .. 16 cb + 15)
+      float zsum;
+      float delta;
+      {
+        const uint4* sp = reinterpret_cast<const uint4*>(km + 32 * cb);
+        const uint4* zp = reinterpret_cast<const uint4*>(km + 256 + 32 * cb);
+        const uint4 s0 = sp[0], s1 = sp[1], z0 = zp[0], z1 = zp[1];
+        const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+        const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+        float w[16];
+        float mx = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          w[2 * j] = mul_f16_f32(uint16_t(qreg[j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
+          w[2 * j + 1] = mul_f16_f32(uint16_t(qreg[j] >> 16), uint16_t(sw[j] >> 16));
+          mx = fmaxf(mx, fmaxf(fabsf(w[2 * j]), fabsf(w[2 * j + 1])));
+        }
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+        mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
+        const float R = mx > 0.f ? __fdividef(kKeyRange, mx) : 0.f;
+        delta = mx * (1.0f / kKeyRange);
+        uint32_t fb[16];
+        zsum = 0.f;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          fb[2 * j] = __float_as_uint(__fmaf_rn(w[2 * j], R, kMagicKey));
+          fb[2 * j + 1] = __float_as_uint(__fmaf_rn(w[2 * j + 1], R, kMagicKey));
+          zsum = __fmaf_rn(h2f(uint16_t(zw[j] & 0xffffu)), w[2 * j], zsum);
+          zsum = __fmaf_rn(h2f(uint16_t(zw[j] >> 16)), w[2 * j + 1], zsum);
+        }
+        zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
+        zsum += __shfl_xor_sync(0xffffffffu, zsum, 2);
+        zsum += __shfl_xor_sync(0xffffffffu, zsum, 4);
+        // position word qq <-> channels 16 cb + qq + {0, 4, 8, 12}
+        uint32_t d0[4], d1[4], d2[4];
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) {
+          bytes01(fb[qq], fb[qq + 4], fb[qq + 8], fb[qq + 12], d0[qq], d1[qq]);
+          d2[qq] = byte2(fb[qq], fb[qq + 4], fb[qq + 8], fb[qq + 12]);
+        }
+        uint8_t* row = dtab + pq * kRow + 16 * cb;
+        *reinterpret_cast<uint4*>(row) = make_uint4(d0[0], d0[1], d0[2], d0[3]);
+        *reinterpret_cast<uint4*>(row + kPlane) = make_uint4(d1[0], d1[1], d1[2], d1[3]);
+        *reinterpret_cast<uint4*>(row + 2 * kPlane) = make_uint4(d2[0], d2[1], d2[2], d2[3]);
+      }
+      __syncwarp();
+      // this lane's query head q_: zero-point term and digit step, from prep lane 8 q_
+      const float zq = __shfl_sync(0xffffffffu, zsum, 8 * q_) * qk_scale;
+      const float cq = __shfl_sync(0xffffffffu, delta, 8 * q_) * qk_scale;
+
+      int acc1[8][4], acc2[8][4];
+#pragma unroll
+      for (int m = 0; m < 8; ++m) {
+        acc1[m][0] = acc1[m][1] = acc1[m][2] = acc1[m][3] = 0;
+        acc2[m][0] = acc2[m][1] = acc2[m][2] = acc2[m][3] = 0;
+      }
+      // ---- baseline plane: K = channels 32 ks + 16 hh + 4 kk + q_ (position 32 ks + 16 hh + 4 q_ + kk)
+#pragma unroll 1
+      for (int ks = 0; ks < 4; ++ks) {
+        uint32_t u[4], v[4], t0[4], t1[4];
+        const uint8_t* r0 = kbuf + (32 * ks + q_) * 32 + 4 * g_;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          u[kk] = lds32(r0 + kk * 4 * 32);
+          v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
+        }
+        transpose4(u, t0);
+        transpose4(v, t1);
+        const uint32_t b10 = lds32(kb1 + 32 * ks + 4 * q_), b11 = lds32(kb1 + 32 * ks + 16 + 4 * q_);
+        const uint32_t b20 = lds32(kb2 + 32 * ks + 4 * q_), b21 = lds32(kb2 + 32 * ks + 16 + 4 * q_);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          // tile 2 jj: tokens 4 jj + 0 (row g_) and 4 jj + 1 (row g_ + 8); tile 2 jj + 1: 4 jj + 2, 4 jj + 3
+          const uint32_t a00 = key_code<0>(t0[jj]), a01 = key_code<1>(t0[jj]);
+          const uint32_t a02 = key_code<0>(t1[jj]), a03 = key_code<1>(t1[jj]);
+          const uint32_t a10 = key_code<2>(t0[jj]), a11 = key_code<3>(t0[jj]);
+          const uint32_t a12 = key_code<2>(t1[jj]), a13 = key_code<3>(t1[jj]);
+          mma_k32(acc1[2 * jj], a00, a01, a02, a03, b10, b11);
+          mma_k32(acc1[2 * jj + 1], a10, a11, a12, a13, b10, b11);
+          mma_k32(acc2[2 * jj], a00, a01, a02, a03, b20, b21);
+          mma_k32(acc2[2 * jj + 1], a10, a11, a12, a13, b20, b21);
+        }
+      }
+      // ---- boosted high plane: K = entries 16 bs + 4 q_ + kk
+      for (int bs = 0; bs < nb; bs += 16) {
+        const uint4 e4 = *reinterpret_cast<const uint4*>(ent + bs + 4 * q_);
+        const uint32_t es[4] = {e4.x, e4.y, e4.z, e4.w};
+        uint32_t u[4], t[4], bb1 = 0u, bb2 = 0u;
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk) {
+          u[kk] = lds32(kh + (es[kk] & 0xffffu) + 4 * g_);
+          const uint32_t pos = es[kk] >> 16;
+          bb1 |= uint32_t(kb1[pos]) << (8 * kk);
+          bb2 |= uint32_t(kb2[pos]) << (8 * kk);
+        }
+        transpose4(u, t);
+#pragma unroll
+        for (int jj = 0; jj < 4; ++jj) {
+          const uint32_t a00 = high_code<0>(t[jj]), a01 = high_code<1>(t[jj]);
+          const uint32_t a10 = high_code<2>(t[jj]), a11 = high_code<3>(t[jj]);
+          mma_k16(acc1[2 * jj], a00, a01, bb1);
+          mma_k16(acc1[2 * jj + 1], a10, a11, bb1);
+          mma_k16(acc2[2 * jj], a00, a01, bb2);
+          mma_k16(acc2[2 * jj + 1], a10, a11, bb2);
+        }
+      }
+      __syncwarp();
+      // keys consumed: request the next page's keys
+      cursor_step(cur, a.num_pages, H);
+      have_next = cursor_to_page(cur, a.num_pages, H, f1);
+      if (lane == 0 && have_next) issue_k(cur);
+
+      // ---- scores (log2 domain) of tokens 16 g_ + v, v = 2 m + hh
+      float s[16];
+      {
+        const float c0 = cq, c1 = cq * 0.25f, c2 = cq * 0.0625f;   // row factors 1, 4, 16, 16
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int lo = 256 * acc1[m][2 * hh] + acc1[m][2 * hh + 1];
+            const int hi = acc2[m][2 * hh] - 64 * acc2[m][2 * hh + 1];
+            const float sx = __fmaf_rn(float(hi), 65536.0f, float(lo));
+            const int i = (2 * m + hh) & 3;
+            const float ci = i == 0 ? c0 : (i == 1 ? c1 : c2);
+            s[2 * m + hh] = __fmaf_rn(sx, ci, -zq);
+          }
+        }
+      }
+
+      if (!mbar_wait(bar_v, v_phase)) { failed = true; break; }
+      v_phase ^= 1u;
+      if (valid) {
+        softmax_step(st, s);   // s -> p
+        // ---- P' = p * scale_v as 16-bit fixed point, tokens 16 g_ + v
+        const uint4* vm4 = reinterpret_cast<const uint4*>(vbuf + 4096 + 64 * g_);
+        uint32_t sz[16];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const uint4 x = vm4[i];
+          sz[4 * i] = x.x; sz[4 * i + 1] = x.y; sz[4 * i + 2] = x.z; sz[4 * i + 3] = x.w;
+        }
+        float pp[16];
+        float mp = 0.f;
+#pragma unroll
+        for (int v = 0; v < 16; ++v) {
+          pp[v] = s[v] * h2f(uint16_t(sz[v] & 0xffffu));
+          mp = fmaxf(mp, pp[v]);
+        }
+        mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 4));
+        mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
+        mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
+        const float Rv = mp > 0.f ? __fdividef(kValRange, mp) : 0.f;
+        const float dv = mp * (1.0f / kValRange);
+        uint32_t yb[16];
+        float zv = 0.f;
+#pragma unroll
+        for (int v = 0; v < 16; ++v) {
+          const float fy = __fmaf_rn(pp[v], Rv, kMagicVal);
+          yb[v] = __float_as_uint(fy);
+          zv = __fmaf_rn(h2f(uint16_t(sz[v] >> 16)), fy - kMagicVal, zv);
+        }
+        st.zs = __fmaf_rn(zv, dv, st.zs);
+        uint32_t y0[4], y1[4];
+#pragma unroll
+        for (int qq = 0; qq < 4; ++qq) bytes01(yb[qq], yb[qq + 4], yb[qq + 8], yb[qq + 12], y0[qq], y1[qq]);
+        uint8_t* prow = ptab + q_ * kRow + 16 * g_;
+        *reinterpret_cast<uint4*>(prow) = make_uint4(y0[0], y0[1], y0[2], y0[3]);
+        *reinterpret_cast<uint4*>(prow + kPlane) = make_uint4(y1[0], y1[1], y1[2], y1[3]);
+        __syncwarp();
+        // ---- values: M = channels, K = tokens 32 ks + 16 hh + 4 kk + q_
+        int acc[8][4];
+#pragma unroll
+        for (int m = 0; m < 8; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0;
+#pragma unroll 1
+        for (int ks = 0; ks < 4; ++ks) {
+          uint32_t u[4], v[4], t0[4], t1[4];
+          const uint8_t* r0 = vbuf + (32 * ks + q_) * 32 + 4 * g_;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            u[kk] = lds32(r0 + kk * 4 * 32);
+            v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
+          }
+          transpose4(u, t0);
+          transpose4(v, t1);
+          const uint32_t b0 = lds32(vb + 32 * ks + 4 * q_), b1 = lds32(vb + 32 * ks + 16 + 4 * q_);
+#pragma unroll
+          for (int jj = 0; jj < 4; ++jj) {
+            mma_k32(acc[2 * jj], val_code<0>(t0[jj]), val_code<1>(t0[jj]), val_code<0>(t1[jj]), val_code<1>(t1[jj]),
+                    b0, b1);
+            mma_k32(acc[2 * jj + 1], val_code<2>(t0[jj]), val_code<3>(t0[jj]), val_code<2>(t1[jj]),
+                    val_code<3>(t1[jj]), b0, b1);
+          }
+        }
+        // ---- accumulate: channel 16 g_ + 2 m + hh, row factor 4^((2 m + hh) & 3)
+        const float e0 = dv, e1 = dv * 0.25f, e2 = dv * 0.0625f, e3 = dv * 0.015625f;
+#pragma unroll
+        for (int m = 0; m < 8; ++m) {
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const int comb = 256 * acc[m][2 * hh] + acc[m][2 * hh + 1];
+            const int i = (2 * m + hh) & 3;
+            const float ei = i == 0 ? e0 : (i == 1 ? e1 : (i == 2 ? e2 : e3));
+            st.o[2 * m + hh] = __fmaf_rn(float(comb), ei, st.o[2 * m + hh]);
+          }
+        }
+      }
+      __syncwarp();
+      // values consumed: request the next page's values
+      if (lane == 0 && have_next) issue_v(cur);
+    }
+
+    // ---- advance; write the partial at a segment end or at the end of the slice
+    ++p;
+    const bool seg_end = p >= a.num_pages[b] + 1;
+    if (seg_end || f + 1 == f1) {
+      float l = st.l, zs = st.zs;
+      l += __shfl_xor_sync(0xffffffffu, l, 4);
+      l += __shfl_xor_sync(0xffffffffu, l, 8);
+      l += __shfl_xor_sync(0xffffffffu, l, 16);
+      zs += __shfl_xor_sync(0xffffffffu, zs, 4);
+      zs += __shfl_xor_sync(0xffffffffu, zs, 8);
+      zs += __shfl_xor_sync(0xffffffffu, zs, 16);
+      const int64_t base = ((int64_t(b) * H + h) * plan.num_splits + slot) * g;
+      if (q_ < g) {
+        float4* o = reinterpret_cast<float4*>(plan.ws_o + (base + q_) * kD + 16 * g_);
+#pragma unroll
+        for (int i = 0; i < 4; ++i)
+          o[i] = make_float4(st.o[4 * i] - zs, st.o[4 * i + 1] - zs, st.o[4 * i + 2] - zs, st.o[4 * i + 3] - zs);
+        if (g_ == 0) {
+          plan.ws_m[base + q_] = st.m == -INFINITY ? -INFINITY : st.m * kLn2;
+          plan.ws_l[base + q_] = l;
+        }
+      }
+      if (seg_end && lane == 0) plan.ws_count[int64_t(b) * H + h] = slot + 1;
+      reset_state(st);
+      if (seg_end && f + 1 < f1) {
+        p = 0;
+        if (++h == H) { h = 0; ++b; }
+        slot = 0;
+        __syncwarp();
+        nb = setup_segment(a, b, h, g, wsm, L, lane, qreg);
+      }
+    }
+  }
+  if (failed) {
+    if (lane == 0) atomicOr(&g_decode_error_i8, 1u);
+    // copies still in flight must land before the CTA's shared memory is released
+    mbar_wait(bar_k, k_phase);
+    mbar_wait(bar_v, v_phase);
+  }
+}
+
+}  // namespace
+
+bool i8_supports(const KittyDecodeArgs& a) {
+  const int g = a.num_q_heads / a.num_kv_heads;
+  auto region_ok = [](const void* p, int64_t s_seq, int64_t s_head, int64_t s_tok) {
+    return p == nullptr || (aligned(p, 16) && s_seq % 8 == 0 && s_head % 8 == 0 && s_tok % 8 == 0);
+  };
+  return a.head_dim == kD && a.group == kG && g >= 1 && g <= 4 && a.d_boost <= 128 &&
+         aligned(a.q, 16) && a.q_s_seq % 8 == 0 && a.q_s_head % 8 == 0 &&
+         region_ok(a.sink_k, a.sk_s_seq, a.sk_s_head, a.sk_s_tok) &&
+         region_ok(a.sink_v, a.sv_s_seq, a.sv_s_head, a.sv_s_tok) &&
+         region_ok(a.tail_k, a.tk_s_seq, a.tk_s_head, a.tk_s_tok) &&
+         region_ok(a.tail_v, a.tv_s_seq, a.tv_s_head, a.tv_s_tok) &&
+         (a.max_pages_per_seq == 0 ||
+          (aligned(a.key_low, 16) && aligned(a.key_meta, 16) && aligned(a.val_codes, 16) &&
+           aligned(a.val_meta, 16) && (a.d_boost == 0 || aligned(a.key_high, 16))));
+}
+
+int i8_ctas_per_sm() { return kCtasPerSm; }
+
+// Same slicing rule as the fp16 tensor-core variant (see mma_plan).
+void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
+  const int items_max = a.max_pages_per_seq + 1;
+  int target = a.num_splits > 0 ? a.num_splits : kSlotsTarget;
+  target = std::max(1, std::min(target, items_max));
+  const int f_min = (items_max + target - 1) / target;
+  plan->pages_per_split = f_min;
+  plan->num_splits = (items_max + f_min - 1) / f_min + 1;
+  const int64_t total_max = int64_t(a.batch) * a.num_kv_heads * items_max;
+  const int64_t warps_needed = (total_max + f_min - 1) / f_min;
+  const int64_t ctas = std::min<int64_t>((warps_needed + kWarps - 1) / kWarps, int64_t(sm_count) * kCtasPerSm);
+  plan->grid = int(std::max<int64_t>(1, ctas));
+}
+
+int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
+  const Layout L = i8_layout(a.d_boost);
+  const int smem = kWarps * L.size;
+  static int configured_bytes = 0;
+  if (configured_bytes < smem) {
+    cudaError_t e = cudaFuncSetAttribute(decode_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    if (e != cudaSuccess) return fail(KITTY_ERR_CUDA, std::string("decode_i8 smem attribute: ") + cudaGetErrorString(e));
+    configured_bytes = smem;
+  }
+  decode_i8_kernel<<<plan.grid, kThreads, smem, stream>>>(a, plan);
+  return check_launch("decode_i8_kernel");
+}
+
+int read_decode_error_i8(uint32_t* flags, int clear) {
+  unsigned int v = 0;
+  cudaError_t e = cudaMemcpyFromSymbol(&v, g_decode_error_i8, sizeof(v));
+  if (e != cudaSuccess) return fail(KITTY_ERR_CUDA, std::string("read error flags: ") + cudaGetErrorString(e));
+  if (clear && v) {
+    const unsigned int zero = 0;
+    e = cudaMemcpyToSymbol(g_decode_error_i8, &zero, sizeof(zero));
+    if (e != cudaSuccess) return fail(KITTY_ERR_CUDA, std::string("clear error flags: ") + cudaGetErrorString(e));
+  }
+  *flags = v;
+  return KITTY_OK;
+}
+
+}  // namespace kitty

@@ -45,12 +45,15 @@
 #include <algorithm>
 
 #include "kitty_decode.cuh"
+#include "kitty_ptx.cuh"
 
 namespace kitty {
 
 __device__ unsigned int g_decode_error = 0;  // bit 0: a bulk-copy wait timed out
 
 namespace {
+
+using namespace dev;
 
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
@@ -79,30 +82,12 @@ __host__ __device__ inline WarpLayout warp_layout(int K) {
   return L;
 }
 
-// ---- PTX helpers ----------------------------------------------------------
+// ---- PTX helpers (fp16 path) ---------------------------------------------
 
-__device__ __forceinline__ uint32_t smem_u32(const void* p) {
-  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
-}
-__device__ __forceinline__ uint32_t prmt(uint32_t a, uint32_t b, uint32_t sel) {
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(sel));
-  return r;
-}
 template <uint32_t kMask>
 __device__ __forceinline__ uint32_t mask_or_magic(uint32_t a) {  // (a & mask) | 1024.0h in both halves
   uint32_t r;
   asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(r) : "r"(a), "n"(kMask), "n"(0x64006400u));
-  return r;
-}
-__device__ __forceinline__ uint32_t hfma2_u32(uint32_t a, uint32_t b, uint32_t c) {
-  uint32_t r;
-  asm("fma.rn.f16x2 %0, %1, %2, %3;" : "=r"(r) : "r"(a), "r"(b), "r"(c));
-  return r;
-}
-__device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
-  uint32_t r;
-  asm("mul.rn.f16x2 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(b));
   return r;
 }
 // x * y as an unevaluated fp16 pair hi + lo: hi = RN(x*y), lo = RN(x*y - hi) (the
@@ -110,16 +95,6 @@ __device__ __forceinline__ uint32_t hmul2_u32(uint32_t a, uint32_t b) {
 __device__ __forceinline__ void hmul2_split(uint32_t x, uint32_t y, uint32_t& hi, uint32_t& lo) {
   hi = hmul2_u32(x, y);
   lo = hfma2_u32(x, y, hi ^ 0x80008000u);
-}
-__device__ __forceinline__ uint32_t pack_f32x2(float lo, float hi) {
-  uint32_t r;
-  asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
-  return r;
-}
-__device__ __forceinline__ float ex2(float x) {
-  float r;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
-  return r;
 }
 __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1) {
@@ -131,30 +106,6 @@ __device__ __forceinline__ void mma16816(float (&c)[4], uint32_t a0, uint32_t a1
 }
 __device__ __forceinline__ void ldmatrix_x2(uint32_t& r0, uint32_t& r1, uint32_t addr) {
   asm volatile("ldmatrix.sync.aligned.m8n8.x2.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(addr));
-}
-__device__ __forceinline__ void mbar_init(uint32_t bar, uint32_t count) {
-  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" :: "r"(bar), "r"(count));
-}
-__device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
-  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" :: "r"(bar), "r"(bytes) : "memory");
-}
-__device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
-  uint32_t ok;
-  asm volatile(
-      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}\n"
-      : "=r"(ok) : "r"(bar), "r"(parity) : "memory");
-  return ok != 0;
-}
-// Bounded wait: gives up after ~2^22 polls (seconds), never spins forever.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity) {
-  for (int i = 0; i < (1 << 22); ++i) {
-    if (mbar_try_wait(bar, parity)) return true;
-  }
-  return false;
-}
-__device__ __forceinline__ void bulk_g2s(uint32_t dst, const void* src, uint32_t bytes, uint32_t bar) {
-  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];"
-               :: "r"(dst), "l"(src), "r"(bytes), "r"(bar) : "memory");
 }
 
 // code (0..3) of byte-slot k of both 16-bit halves of u, as exact fp16x2
@@ -192,10 +143,6 @@ __device__ __forceinline__ void plane_kstep(float (&acc)[8][4], uint32_t w0, uin
   KITTY_MTILE(4, 0) KITTY_MTILE(5, 1) KITTY_MTILE(6, 2) KITTY_MTILE(7, 3)
 #undef KITTY_MTILE
 }
-
-__device__ __forceinline__ uint32_t lds32(const uint8_t* p) { return *reinterpret_cast<const uint32_t*>(p); }
-__device__ __forceinline__ uint32_t lds16(const uint8_t* p) { return *reinterpret_cast<const uint16_t*>(p); }
-__device__ __forceinline__ uint32_t pack16(uint32_t lo, uint32_t hi) { return lo | (hi << 16); }
 
 struct WarpState {
   float o[8][4];     // O^T C fragments: channel rows, query-head columns 2*q_, 2*q_+1
@@ -265,47 +212,6 @@ __device__ __forceinline__ void softmax_and_stage(WarpState& st, float (&s)[8][4
 __device__ __forceinline__ void load_pfrag(uint32_t& b0, uint32_t& b1, const __half* ps, int s, int lane) {
   const int mi = (lane >> 3) & 1, n = lane & 7;
   ldmatrix_x2(b0, b1, smem_u32(ps + n * kPRow + 16 * s + 8 * mi));
-}
-
-struct SegmentScan {
-  int64_t total;     // items over all segments
-  int64_t seg_begin; // for the located item: start of its segment
-  int b, h, p;       // located item: sequence, KV head, item index in the segment
-};
-
-// Warp-cooperative: total item count and the (b, h, p) of item f (when f < total).
-// Segment (b, h) has L_b = num_pages[b] + 1 items; sequence b's segments start at
-// H * sum_{b' < b} L_b'.
-__device__ SegmentScan scan_segments(const int32_t* num_pages, int B, int H, int64_t f, int lane) {
-  SegmentScan r;
-  r.b = -1; r.h = 0; r.p = 0; r.seg_begin = 0;
-  int64_t run = 0;
-  for (int b0 = 0; b0 < B; b0 += 32) {
-    const int b = b0 + lane;
-    const int64_t seq_items = (b < B) ? int64_t(H) * (int64_t(max(num_pages[b], 0)) + 1) : 0;
-    int64_t incl = seq_items;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int64_t v = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += v;
-    }
-    const int64_t start = run + incl - seq_items;
-    const bool hit = (b < B) && (f >= start) && (f < start + seq_items);
-    const uint32_t bal = __ballot_sync(0xffffffffu, hit);
-    if (bal != 0u && r.b < 0) {
-      const int src = __ffs(bal) - 1;
-      const int64_t st = __shfl_sync(0xffffffffu, start, src);
-      const int bb = b0 + src;
-      const int64_t L = int64_t(max(num_pages[bb], 0)) + 1;
-      r.b = bb;
-      r.h = int((f - st) / L);
-      r.p = int((f - st) - int64_t(r.h) * L);
-      r.seg_begin = st + int64_t(r.h) * L;
-    }
-    run += __shfl_sync(0xffffffffu, incl, 31);
-  }
-  r.total = run;
-  return r;
 }
 
 // Query rows of (b, h) and the boosted-channel list of head h into the warp's
@@ -439,26 +345,6 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, Warp
     }
     __syncwarp();
   }
-}
-
-// Producer cursor over the real pages of a warp's slice.
-struct Cursor {
-  int64_t f;   // item index
-  int b, h, p; // sequence, KV head, item in segment (p >= 1: page p - 1)
-};
-
-__device__ __forceinline__ void cursor_step(Cursor& c, const int32_t* num_pages, int H) {
-  ++c.f; ++c.p;
-  if (c.p >= num_pages[c.b] + 1) { c.p = 0; if (++c.h == H) { c.h = 0; ++c.b; } }
-}
-
-// advance to the next real page in [c.f, end); false if none
-__device__ __forceinline__ bool cursor_to_page(Cursor& c, const int32_t* num_pages, int H, int64_t end) {
-  while (c.f < end) {
-    if (c.p >= 1) return true;
-    cursor_step(c, num_pages, H);
-  }
-  return false;
 }
 
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)

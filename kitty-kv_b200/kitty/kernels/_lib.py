@@ -83,6 +83,7 @@ SIGNATURES = {
     "kitty_paged_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
     "kitty_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "kitty_paged_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
+    "kitty_decode_force_variant": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
 }
 STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs}
 
@@ -132,6 +133,18 @@ def device_error_flags(clear: bool = True) -> int:
     v = ctypes.c_uint32(0)
     check(load().kitty_device_error_flags(ctypes.byref(v), int(clear)), "kitty_device_error_flags")
     return v.value
+
+
+DECODE_VARIANTS = {"auto": -1, "simt": 0, "mma": 1, "int8": 2}
+
+
+def force_decode_variant(name: str) -> str:
+    """Pin the decode kernel family ("auto", "simt", "mma" or "int8") for later decode
+    calls of this process; returns the previous setting.  Shapes the pinned family
+    does not support fall back to the library's choice."""
+    prev = ctypes.c_int(-1)
+    check(load().kitty_decode_force_variant(DECODE_VARIANTS[name], ctypes.byref(prev)), "kitty_decode_force_variant")
+    return {v: k for k, v in DECODE_VARIANTS.items()}[prev.value]
 
 
 def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:

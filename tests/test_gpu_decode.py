@@ -119,13 +119,22 @@ def test_empty_context_gives_zeros():
     assert torch.count_nonzero(out).item() == 0
 
 
+@pytest.fixture(params=["auto", "simt", "mma", "int8"])
+def variant(request):
+    """Each decode kernel family pinned in turn (shapes a family does not support fall
+    back to the library's choice)."""
+    prev = KK._lib.force_decode_variant(request.param)
+    yield request.param
+    KK._lib.force_decode_variant(prev)
+
+
 @pytest.mark.parametrize("seed,B,Hq,H,ctx,rate", [
     (101, 4, 32, 8, [32 + 40 * 128 + 77, 32 + 3 * 128, 300, 32 + 17 * 128 + 1], 0.125),
     (102, 3, 64, 8, [32 + 9 * 128 + 96, 32 + 21 * 128 + 5, 32 + 2 * 128 + 127], 0.125),   # GQA 8:1
     (103, 2, 8, 8, [32 + 6 * 128 + 3, 32 + 11 * 128 + 64], 0.25),                            # MHA, K=32
     (104, 2, 16, 2, [32 + 64 * 128 + 10, 40], 0.25),
 ])
-def test_random_batches_vs_oracle(seed, B, Hq, H, ctx, rate):
+def test_random_batches_vs_oracle(seed, B, Hq, H, ctx, rate, variant):
     case = synthetic.make_decode_case(seed, B, Hq, H, 128, ctx, boost_rate=rate)
     total = sum(s.n_pages for s in case.seqs)
     n_phys = total + 5
