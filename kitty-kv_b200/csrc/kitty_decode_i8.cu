@@ -101,6 +101,20 @@ __device__ __forceinline__ void mma_k32(int (&c)[4], uint32_t a0, uint32_t a1, u
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
+// first k-step of an accumulation: C = 0 (no accumulator initialisation)
+__device__ __forceinline__ void mma_k32_z(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                          uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k32.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+      : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+}
+template <bool kFirst>
+__device__ __forceinline__ void mma_k32_acc(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                            uint32_t b0, uint32_t b1) {
+  if (kFirst) mma_k32_z(c, a0, a1, a2, a3, b0, b1);
+  else mma_k32(c, a0, a1, a2, a3, b0, b1);
+}
 __device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
   asm volatile(
       "mma.sync.aligned.m16n8k16.row.col.s32.u8.u8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
@@ -152,6 +166,66 @@ __device__ __forceinline__ void bytes01(uint32_t v0, uint32_t v1, uint32_t v2, u
 __device__ __forceinline__ uint32_t byte2(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
   return prmt(prmt(v0, v1, 0x0062u), prmt(v2, v3, 0x0062u), 0x5410u);
 }
+// fp16 pair (low half first) -> float2
+__device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
+  __half2 h;
+  memcpy(&h, &v, 4);
+  return __half22float2(h);
+}
+// One 32-channel k-step of the key baseline plane (channels 32 ks + 16 hh + 4 kk + q_,
+// positions 32 ks + 16 hh + 4 q_ + kk) into the 8 token tiles.
+template <bool kFirst>
+__device__ __forceinline__ void key_kstep(int (&acc1)[8][4], int (&acc2)[8][4], const uint8_t* kbuf, const uint8_t* kb1,
+                                          const uint8_t* kb2, int ks, int g_, int q_) {
+  uint32_t u[4], v[4], t0[4], t1[4];
+  const uint8_t* r0 = kbuf + (32 * ks + q_) * 32 + 4 * g_;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    u[kk] = lds32(r0 + kk * 4 * 32);
+    v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
+  }
+  transpose4(u, t0);
+  transpose4(v, t1);
+  const uint32_t b10 = lds32(kb1 + 32 * ks + 4 * q_), b11 = lds32(kb1 + 32 * ks + 16 + 4 * q_);
+  const uint32_t b20 = lds32(kb2 + 32 * ks + 4 * q_), b21 = lds32(kb2 + 32 * ks + 16 + 4 * q_);
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    // tile 2 jj: tokens 4 jj + 0 (row g_) and 4 jj + 1 (row g_ + 8); tile 2 jj + 1: 4 jj + 2, 4 jj + 3
+    const uint32_t a00 = key_code<0>(t0[jj]), a01 = key_code<1>(t0[jj]);
+    const uint32_t a02 = key_code<0>(t1[jj]), a03 = key_code<1>(t1[jj]);
+    const uint32_t a10 = key_code<2>(t0[jj]), a11 = key_code<3>(t0[jj]);
+    const uint32_t a12 = key_code<2>(t1[jj]), a13 = key_code<3>(t1[jj]);
+    mma_k32_acc<kFirst>(acc1[2 * jj], a00, a01, a02, a03, b10, b11);
+    mma_k32_acc<kFirst>(acc1[2 * jj + 1], a10, a11, a12, a13, b10, b11);
+    mma_k32_acc<kFirst>(acc2[2 * jj], a00, a01, a02, a03, b20, b21);
+    mma_k32_acc<kFirst>(acc2[2 * jj + 1], a10, a11, a12, a13, b20, b21);
+  }
+}
+
+// One 32-token k-step of the value plane (tokens 32 ks + 16 hh + 4 kk + q_) into the 8
+// channel tiles.
+template <bool kFirst>
+__device__ __forceinline__ void val_kstep(int (&acc)[8][4], const uint8_t* vbuf, const uint8_t* vb, int ks, int g_,
+                                          int q_) {
+  uint32_t u[4], v[4], t0[4], t1[4];
+  const uint8_t* r0 = vbuf + (32 * ks + q_) * 32 + 4 * g_;
+#pragma unroll
+  for (int kk = 0; kk < 4; ++kk) {
+    u[kk] = lds32(r0 + kk * 4 * 32);
+    v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
+  }
+  transpose4(u, t0);
+  transpose4(v, t1);
+  const uint32_t b0 = lds32(vb + 32 * ks + 4 * q_), b1 = lds32(vb + 32 * ks + 16 + 4 * q_);
+#pragma unroll
+  for (int jj = 0; jj < 4; ++jj) {
+    mma_k32_acc<kFirst>(acc[2 * jj], val_code<0>(t0[jj]), val_code<1>(t0[jj]), val_code<0>(t1[jj]),
+                        val_code<1>(t1[jj]), b0, b1);
+    mma_k32_acc<kFirst>(acc[2 * jj + 1], val_code<2>(t0[jj]), val_code<3>(t0[jj]), val_code<2>(t1[jj]),
+                        val_code<3>(t1[jj]), b0, b1);
+  }
+}
+
 // permuted K position of channel / token c (see the header comment)
 __device__ __forceinline__ int kpos(int c) { return (c & ~15) | ((c & 3) << 2) | ((c >> 2) & 3); }
 
@@ -180,20 +254,31 @@ __device__ __forceinline__ void softmax_step(State& st, float (&s)[16]) {
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
   const float mn = fmaxf(st.m, mx);
+  const bool moved = mn > st.m;   // false while the running max holds (and for -inf == -inf)
   const float alpha = (st.m == -INFINITY) ? 0.f : ex2(st.m - mn);
   // a fully masked chunk before any real token keeps everything at zero
   const float base = (mn == -INFINITY) ? 0.f : mn;
   st.m = mn;
-  float sum = 0.f;
+  float2 sum = make_float2(0.f, 0.f);
 #pragma unroll
-  for (int v = 0; v < 16; ++v) {
-    s[v] = ex2(s[v] - base);
-    sum += s[v];
+  for (int v = 0; v < 16; v += 2) {
+    const float2 d = add2(make_float2(s[v], s[v + 1]), make_float2(-base, -base));
+    s[v] = ex2(d.x);
+    s[v + 1] = ex2(d.y);
+    sum = add2(sum, make_float2(s[v], s[v + 1]));
   }
-  st.l = st.l * alpha + sum;
-  st.zs *= alpha;
+  // once the running maxima settle, no lane rescales: skip the accumulator update
+  if (__any_sync(0xffffffffu, moved)) {
+    st.l *= alpha;
+    st.zs *= alpha;
 #pragma unroll
-  for (int v = 0; v < 16; ++v) st.o[v] *= alpha;
+    for (int v = 0; v < 16; v += 2) {
+      const float2 o = mul2(make_float2(st.o[v], st.o[v + 1]), make_float2(alpha, alpha));
+      st.o[v] = o.x;
+      st.o[v + 1] = o.y;
+    }
+  }
+  st.l += sum.x + sum.y;
 }
 
 // Per-segment setup: q of the prep lane's (query head, 16 channels) and the
@@ -462,14 +547,16 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         const float R = mx > 0.f ? __fdividef(kKeyRange, mx) : 0.f;
         delta = mx * (1.0f / kKeyRange);
         uint32_t fb[16];
-        zsum = 0.f;
+        float2 zs2 = make_float2(0.f, 0.f);
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          fb[2 * j] = __float_as_uint(__fmaf_rn(w[2 * j], R, kMagicKey));
-          fb[2 * j + 1] = __float_as_uint(__fmaf_rn(w[2 * j + 1], R, kMagicKey));
-          zsum = __fmaf_rn(h2f(uint16_t(zw[j] & 0xffffu)), w[2 * j], zsum);
-          zsum = __fmaf_rn(h2f(uint16_t(zw[j] >> 16)), w[2 * j + 1], zsum);
+          const float2 wj = make_float2(w[2 * j], w[2 * j + 1]);
+          const float2 f = fma2(wj, make_float2(R, R), make_float2(kMagicKey, kMagicKey));
+          fb[2 * j] = __float_as_uint(f.x);
+          fb[2 * j + 1] = __float_as_uint(f.y);
+          zs2 = fma2(h2_to_f2(zw[j]), wj, zs2);
         }
+        zsum = zs2.x + zs2.y;
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 2);
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 4);
@@ -491,38 +578,10 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       const float cq = __shfl_sync(0xffffffffu, delta, 8 * q_) * qk_scale;
 
       int acc1[8][4], acc2[8][4];
-#pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        acc1[m][0] = acc1[m][1] = acc1[m][2] = acc1[m][3] = 0;
-        acc2[m][0] = acc2[m][1] = acc2[m][2] = acc2[m][3] = 0;
-      }
-      // ---- baseline plane: K = channels 32 ks + 16 hh + 4 kk + q_ (position 32 ks + 16 hh + 4 q_ + kk)
+      // ---- baseline plane
+      key_kstep<true>(acc1, acc2, kbuf, kb1, kb2, 0, g_, q_);
 #pragma unroll 1
-      for (int ks = 0; ks < 4; ++ks) {
-        uint32_t u[4], v[4], t0[4], t1[4];
-        const uint8_t* r0 = kbuf + (32 * ks + q_) * 32 + 4 * g_;
-#pragma unroll
-        for (int kk = 0; kk < 4; ++kk) {
-          u[kk] = lds32(r0 + kk * 4 * 32);
-          v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
-        }
-        transpose4(u, t0);
-        transpose4(v, t1);
-        const uint32_t b10 = lds32(kb1 + 32 * ks + 4 * q_), b11 = lds32(kb1 + 32 * ks + 16 + 4 * q_);
-        const uint32_t b20 = lds32(kb2 + 32 * ks + 4 * q_), b21 = lds32(kb2 + 32 * ks + 16 + 4 * q_);
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          // tile 2 jj: tokens 4 jj + 0 (row g_) and 4 jj + 1 (row g_ + 8); tile 2 jj + 1: 4 jj + 2, 4 jj + 3
-          const uint32_t a00 = key_code<0>(t0[jj]), a01 = key_code<1>(t0[jj]);
-          const uint32_t a02 = key_code<0>(t1[jj]), a03 = key_code<1>(t1[jj]);
-          const uint32_t a10 = key_code<2>(t0[jj]), a11 = key_code<3>(t0[jj]);
-          const uint32_t a12 = key_code<2>(t1[jj]), a13 = key_code<3>(t1[jj]);
-          mma_k32(acc1[2 * jj], a00, a01, a02, a03, b10, b11);
-          mma_k32(acc1[2 * jj + 1], a10, a11, a12, a13, b10, b11);
-          mma_k32(acc2[2 * jj], a00, a01, a02, a03, b20, b21);
-          mma_k32(acc2[2 * jj + 1], a10, a11, a12, a13, b20, b21);
-        }
-      }
+      for (int ks = 1; ks < 4; ++ks) key_kstep<false>(acc1, acc2, kbuf, kb1, kb2, ks, g_, q_);
       // ---- boosted high plane: K = entries 16 bs + 4 q_ + kk
       for (int bs = 0; bs < nb; bs += 16) {
         const uint4 e4 = *reinterpret_cast<const uint4*>(ent + bs + 4 * q_);
@@ -555,18 +614,17 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       // ---- scores (log2 domain) of tokens 16 g_ + v, v = 2 m + hh
       float s[16];
       {
-        const float c0 = cq, c1 = cq * 0.25f, c2 = cq * 0.0625f;   // row factors 1, 4, 16, 16
+        // row factors 1, 4, 16, 16 for token 2 m + hh: tiles with m even hold i = 0, 1, odd i = 2, 3
+        const float2 ce = make_float2(cq, cq * 0.25f), co = make_float2(cq * 0.0625f, cq * 0.0625f);
+        const float2 ce16 = make_float2(ce.x * 65536.0f, ce.y * 65536.0f), co16 = make_float2(co.x * 65536.0f, co.y * 65536.0f);
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int lo = 256 * acc1[m][2 * hh] + acc1[m][2 * hh + 1];
-            const int hi = acc2[m][2 * hh] - 64 * acc2[m][2 * hh + 1];
-            const float sx = __fmaf_rn(float(hi), 65536.0f, float(lo));
-            const int i = (2 * m + hh) & 3;
-            const float ci = i == 0 ? c0 : (i == 1 ? c1 : c2);
-            s[2 * m + hh] = __fmaf_rn(sx, ci, -zq);
-          }
+          const int lo0 = 256 * acc1[m][0] + acc1[m][1], lo1 = 256 * acc1[m][2] + acc1[m][3];
+          const int hi0 = acc2[m][0] - 64 * acc2[m][1], hi1 = acc2[m][2] - 64 * acc2[m][3];
+          const float2 t = fma2(make_float2(float(lo0), float(lo1)), (m & 1) ? co : ce, make_float2(-zq, -zq));
+          const float2 r = fma2(make_float2(float(hi0), float(hi1)), (m & 1) ? co16 : ce16, t);
+          s[2 * m] = r.x;
+          s[2 * m + 1] = r.y;
         }
       }
 
@@ -585,9 +643,13 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         float pp[16];
         float mp = 0.f;
 #pragma unroll
-        for (int v = 0; v < 16; ++v) {
-          pp[v] = s[v] * h2f(uint16_t(sz[v] & 0xffffu));
-          mp = fmaxf(mp, pp[v]);
+        for (int v = 0; v < 16; v += 2) {
+          // (scale, zero) of tokens v and v + 1 -> (scale_v, scale_v+1)
+          const float2 sc = h2_to_f2(prmt(sz[v], sz[v + 1], 0x5410u));
+          const float2 pr = mul2(make_float2(s[v], s[v + 1]), sc);
+          pp[v] = pr.x;
+          pp[v + 1] = pr.y;
+          mp = fmaxf(mp, fmaxf(pr.x, pr.y));
         }
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 4));
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
@@ -595,13 +657,17 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         const float Rv = mp > 0.f ? __fdividef(kValRange, mp) : 0.f;
         const float dv = mp * (1.0f / kValRange);
         uint32_t yb[16];
-        float zv = 0.f;
+        float2 zv2 = make_float2(0.f, 0.f);
 #pragma unroll
-        for (int v = 0; v < 16; ++v) {
-          const float fy = __fmaf_rn(pp[v], Rv, kMagicVal);
-          yb[v] = __float_as_uint(fy);
-          zv = __fmaf_rn(h2f(uint16_t(sz[v] >> 16)), fy - kMagicVal, zv);
+        for (int v = 0; v < 16; v += 2) {
+          const float2 fy = fma2(make_float2(pp[v], pp[v + 1]), make_float2(Rv, Rv), make_float2(kMagicVal, kMagicVal));
+          yb[v] = __float_as_uint(fy.x);
+          yb[v + 1] = __float_as_uint(fy.y);
+          const float2 y = add2(fy, make_float2(-kMagicVal, -kMagicVal));
+          const uint32_t zz = prmt(sz[v], sz[v + 1], 0x7632u);   // zero-points of tokens v, v + 1
+          zv2 = fma2(h2_to_f2(zz), y, zv2);
         }
+        const float zv = zv2.x + zv2.y;
         st.zs = __fmaf_rn(zv, dv, st.zs);
         uint32_t y0[4], y1[4];
 #pragma unroll
@@ -612,39 +678,18 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         __syncwarp();
         // ---- values: M = channels, K = tokens 32 ks + 16 hh + 4 kk + q_
         int acc[8][4];
-#pragma unroll
-        for (int m = 0; m < 8; ++m) acc[m][0] = acc[m][1] = acc[m][2] = acc[m][3] = 0;
+        val_kstep<true>(acc, vbuf, vb, 0, g_, q_);
 #pragma unroll 1
-        for (int ks = 0; ks < 4; ++ks) {
-          uint32_t u[4], v[4], t0[4], t1[4];
-          const uint8_t* r0 = vbuf + (32 * ks + q_) * 32 + 4 * g_;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            u[kk] = lds32(r0 + kk * 4 * 32);
-            v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
-          }
-          transpose4(u, t0);
-          transpose4(v, t1);
-          const uint32_t b0 = lds32(vb + 32 * ks + 4 * q_), b1 = lds32(vb + 32 * ks + 16 + 4 * q_);
-#pragma unroll
-          for (int jj = 0; jj < 4; ++jj) {
-            mma_k32(acc[2 * jj], val_code<0>(t0[jj]), val_code<1>(t0[jj]), val_code<0>(t1[jj]), val_code<1>(t1[jj]),
-                    b0, b1);
-            mma_k32(acc[2 * jj + 1], val_code<2>(t0[jj]), val_code<3>(t0[jj]), val_code<2>(t1[jj]),
-                    val_code<3>(t1[jj]), b0, b1);
-          }
-        }
+        for (int ks = 1; ks < 4; ++ks) val_kstep<false>(acc, vbuf, vb, ks, g_, q_);
         // ---- accumulate: channel 16 g_ + 2 m + hh, row factor 4^((2 m + hh) & 3)
-        const float e0 = dv, e1 = dv * 0.25f, e2 = dv * 0.0625f, e3 = dv * 0.015625f;
+        const float2 ee = make_float2(dv, dv * 0.25f), eo = make_float2(dv * 0.0625f, dv * 0.015625f);
 #pragma unroll
         for (int m = 0; m < 8; ++m) {
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const int comb = 256 * acc[m][2 * hh] + acc[m][2 * hh + 1];
-            const int i = (2 * m + hh) & 3;
-            const float ei = i == 0 ? e0 : (i == 1 ? e1 : (i == 2 ? e2 : e3));
-            st.o[2 * m + hh] = __fmaf_rn(float(comb), ei, st.o[2 * m + hh]);
-          }
+          const int c0 = 256 * acc[m][0] + acc[m][1], c1 = 256 * acc[m][2] + acc[m][3];
+          const float2 o = fma2(make_float2(float(c0), float(c1)), (m & 1) ? eo : ee,
+                                make_float2(st.o[2 * m], st.o[2 * m + 1]));
+          st.o[2 * m] = o.x;
+          st.o[2 * m + 1] = o.y;
         }
       }
       __syncwarp();
@@ -736,7 +781,24 @@ int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStrea
     if (e != cudaSuccess) return fail(KITTY_ERR_CUDA, std::string("decode_i8 smem attribute: ") + cudaGetErrorString(e));
     configured_bytes = smem;
   }
-  decode_i8_kernel<<<plan.grid, kThreads, smem, stream>>>(a, plan);
+  // persistent grid: no more CTAs than fit on the GPU at once (shared memory grows with d_boost)
+  static int occ_smem = -1, occ_blocks = kCtasPerSm;
+  if (occ_smem != smem) {
+    int n = 0;
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel, kThreads, smem) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = 1;
+    }
+    occ_blocks = std::min(n, kCtasPerSm);
+    occ_smem = smem;
+  }
+  int dev = 0, sms = 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+    cudaGetLastError();
+    sms = 148;
+  }
+  const int grid = std::max(1, std::min(plan.grid, sms * occ_blocks));
+  decode_i8_kernel<<<grid, kThreads, smem, stream>>>(a, plan);
   return check_launch("decode_i8_kernel");
 }
 
