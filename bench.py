@@ -40,6 +40,13 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "kitty-kv_b200"))
 
 METRIC = "quantized paged decode-attn HBM GB/s (% of peak) & tokens/s at 1/2/4/8 B200"
+# DRAM bytes (read + write) of one decode launch, from one ncu capture
+# (dram__bytes_read.sum + dram__bytes_write.sum) of this script on the same workload
+# and kernel; None where no capture exists.
+MEASURED_TRAFFIC = {
+    ("config2", "decode_i8_kernel"): 652_401_408 + 5_087_744,
+    ("config2", "decode_mma_kernel"): 652_734_720 + 5_091_328,
+}
 
 WORKLOADS = {
     # name: batch, q heads, kv heads, head_dim, context, boost_rate
@@ -313,8 +320,11 @@ def kitty_arm(args, spec):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         return float(t.item())
 
+    from kitty.kernels import _lib
+    _lib.force_decode_variant(args.variant)
     w = build_workload(spec, device, seed=1234 + rank)
     B, Hq, H, D, G, K = w["B"], w["Hq"], w["H"], w["D"], w["G"], w["K"]
+    kernel = decode_kernel_name(args.variant, Hq // H, D, G)
     nbytes = algorithmic_bytes(B, Hq, H, D, G, K, w["n_pages"], SINK, w["tail"])
     stream = torch.cuda.current_stream(device)
     out = torch.empty(B, Hq, D, dtype=torch.float16, device=device)
@@ -419,8 +429,8 @@ def kitty_arm(args, spec):
             "e2e": {"value": round(nbytes * world / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                     "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                         "frac": round(achieved / peak, 4), "traffic": None,
-                         "peak_source": f"{peak_kind} copy bandwidth", "kernel": "decode (+ split merge)",
+                         "frac": round(achieved / peak, 4), "traffic": MEASURED_TRAFFIC.get((args.workload, kernel)),
+                         "peak_source": f"{peak_kind} copy bandwidth", "kernel": f"{kernel} (+ split merge)",
                          "algorithmic_bytes_per_launch": nbytes},
             "cpu_baseline": cpu,
             "clocks": clocks.summary(),
@@ -431,6 +441,14 @@ def kitty_arm(args, spec):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def decode_kernel_name(variant, g, D, G):
+    """Kernel family a decode call runs (the library's choice for "auto")."""
+    if variant == "auto":
+        variant = "int8" if (D == 128 and G == 128 and g <= 4) else ("mma" if (D == 128 and G == 128 and g <= 8)
+                                                                      else "simt")
+    return {"int8": "decode_i8_kernel", "mma": "decode_mma_kernel", "simt": "decode_simt_kernel"}[variant]
 
 
 def _decode_args_for_plan(w):
@@ -455,6 +473,9 @@ def main():
     ap.add_argument("--impl", choices=["kitty", "reference"], default="kitty")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--variant", choices=["auto", "simt", "mma", "int8"], default="auto",
+                    help="decode kernel family (auto: integer tensor-core kernel for <= 4 query heads per "
+                         "KV head, fp16 tensor-core kernel up to 8, CUDA-core kernel otherwise)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     spec = WORKLOADS[args.workload]
