@@ -231,6 +231,8 @@ __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
 // ---------------------------------------------------------------------------
 
 constexpr int kFastThreads = 256;
+constexpr float kMagic = 12582912.0f;          // 1.5 * 2^23: fma(x, r, kMagic + zp) = kMagic + zp + rint(x r)
+constexpr float kNearHalf = 0.49996948f;       // 0.5 - 2^-15
 
 struct Tile8x8 {
   uint4 row[8];  // row[i] = 8 channels (fp16) of token 8*tg + i
@@ -265,22 +267,75 @@ __device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
   return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
 }
 
-// code of x (fp32 of an fp16) with the reference's arithmetic; fast clamps when the
-// channel / token statistics are finite (then every element is finite too)
-__device__ __forceinline__ uint32_t quant_code(float x, float scale, float zp, float maxq, bool finite) {
+// code of x (fp32 of an fp16) with the reference's arithmetic, exact IEEE division;
+// handles non-finite statistics (NaN codes become 0)
+__device__ __forceinline__ uint32_t quant_code(float x, float scale, float zp, float maxq) {
   float q = rintf(__fdiv_rn(x, scale)) + zp;
-  if (finite) return static_cast<uint32_t>(fminf(fmaxf(q, 0.0f), maxq));
   q = tmin(tmax(q, 0.0f), maxq);
   return to_code(q);
 }
 
-__global__ void __launch_bounds__(kFastThreads)
+// Fast codes of an fp16 pair.  fma(x, r, kMagic + zp) with r = __frcp_rn(scale) holds
+// kMagic + zp + rint(x r) (one rounding of the exact product); x r is within
+// 2^-23 |x / scale| of the correctly rounded quotient, so rint agrees with the
+// reference's rintf(x / scale) unless x r is within 2^-15 of a half-integer (for
+// |x / scale| < 64; beyond that every rounding clamps to the same code).  Such
+// elements - in practice quotients that are exact half-integers, ~1e-4 of the
+// elements - set their bit in the near-tie masks (bits b0, b1) and are recomputed
+// with the exact division by the caller.  The clamp to [0, maxq] is taken on the
+// biased floats, so the low byte of each result is the code.  Statistics must be
+// finite.
+__device__ __forceinline__ void fast_pair(uint32_t hx, float2 r, float2 mz, float2 top, uint32_t& mask, uint32_t b0,
+                                          uint32_t b1, uint32_t& c0, uint32_t& c1) {
+  const float2 x = __half22float2(u2h2(hx));
+  const float f0 = __fmaf_rn(x.x, r.x, mz.x), f1 = __fmaf_rn(x.y, r.y, mz.y);
+  const float e0 = __fmaf_rn(x.x, r.x, mz.x - f0), e1 = __fmaf_rn(x.y, r.y, mz.y - f1);   // x r - rint(x r)
+  if (fabsf(e0) > kNearHalf) mask |= b0;
+  if (fabsf(e1) > kNearHalf) mask |= b1;
+  c0 = __float_as_uint(fminf(fmaxf(f0, kMagic), top.x));
+  c1 = __float_as_uint(fminf(fmaxf(f1, kMagic), top.y));
+}
+
+// Exact codes of the flagged elements of one 8-element row (bit j of `flags` =
+// element j; element j's fp16 value at src[j * stride]); patches the 2-bit fields
+// of lo (bits 0-1 of each code) and hi (bits 2-3).  Rare: kept out of line.
+__device__ __noinline__ uint2 patch_row(uint32_t flags, const uint16_t* src, int64_t stride, float scale, float zp,
+                                        float maxq, uint32_t lo, uint32_t hi) {
+  for (int j = 0; j < 8; ++j) {
+    if (!((flags >> j) & 1u)) continue;
+    const uint32_t code = quant_code(h2f(src[j * stride]), scale, zp, maxq);
+    lo = (lo & ~(3u << (2 * j))) | ((code & 3u) << (2 * j));
+    hi = (hi & ~(3u << (2 * j))) | (((code >> 2) & 3u) << (2 * j));
+  }
+  return make_uint2(lo, hi);
+}
+
+// four codes (low bytes of c0..c3) -> bits 0-1 of each into one byte (code k at 2k)
+__device__ __forceinline__ uint32_t pack4(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, int shift) {
+  uint32_t w;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(w) : "r"(c0), "r"(c1));
+  uint32_t w2;
+  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(w2) : "r"(c2), "r"(c3));
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w) : "r"(w), "r"(w2));
+  w = (w >> shift) & 0x03030303u;
+  // x (2^24 + 2^18 + 2^12 + 2^6) puts b0 + 4 b1 + 16 b2 + 64 b3 in bits 24..31; the
+  // other partial products stay below 2^24 (at most 3 * 5525568) or wrap past 2^32
+  return (w * 0x01041040u) >> 24;
+}
+
+// low plane byte of channel c, token word j (tokens 4j..4j+3) in the swizzled
+// shared staging: 32-bit word (j / 4) ^ (c >> 3 & 7) of row c
+__device__ __forceinline__ int low_swz(int c, int byte) {
+  return c * 32 + ((((byte >> 2) ^ (c >> 3)) & 7) << 2) + (byte & 3);
+}
+
+__global__ void __launch_bounds__(kFastThreads, 4)
 quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
   constexpr int D = 128, G = 128, G4 = 32;
   __shared__ __align__(16) uint32_t s_red[8][64][2];   // per warp, per channel pair: (min, max) half2
-  __shared__ float s_scale[D], s_zp[D], s_maxq[D];
+  __shared__ float s_scale[D], s_zp[D], s_maxq[D], s_r[D];
   __shared__ int s_row[D];
-  __shared__ int s_finite[D];
+  __shared__ int s_nonfinite;
   __shared__ __align__(16) uint8_t s_low[D * G4];
   __shared__ __align__(16) uint32_t s_high[128 * G4 / 4];
   const int K = a.d_boost;
@@ -294,6 +349,7 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
   Tile8x8 t;
   load_tile(t, src, a.key_s_tok, tg, cg, G);
   for (int i = tid; i < K * G4 / 4; i += kFastThreads) s_high[i] = 0u;
+  if (tid == 0) s_nonfinite = 0;
 
   // per channel-pair min / max over this thread's 8 tokens
   __half2 mn[4], mx[4];
@@ -330,6 +386,7 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
     }
     uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.key_scale) + page * a.meta_s_page + h * a.meta_s_head;
     uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.key_zero) + page * a.meta_s_page + h * a.meta_s_head;
+    bool nonfinite = false;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int c = 2 * tid + e;
@@ -341,46 +398,81 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
       const float scale = __fdiv_rn(clamp_min(mxf - mnf, 1e-8f), maxq);
       float zp = rintf(__fdiv_rn(-mnf, scale));
       zp = tmin(tmax(zp, 0.0f), maxq);
-      s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq;
+      s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq; s_r[c] = __frcp_rn(scale);
       s_row[c] = (boosted && r < K) ? r : -1;
-      s_finite[c] = isfinite(mnf) && isfinite(mxf) && isfinite(scale);
+      nonfinite |= !(isfinite(mnf) && isfinite(mxf) && isfinite(scale));
       out_scale[c] = f2h(scale);
       out_zero[c] = f2h(zp);
     }
+    if (nonfinite) s_nonfinite = 1;
   }
   __syncthreads();
 
-  // quantise: channel c = 8*cg + k, bytes (c, 2*tg) and (c, 2*tg+1)
-#pragma unroll
-  for (int k = 0; k < 8; ++k) {
-    const int c = 8 * cg + k;
-    const float scale = s_scale[c], zp = s_zp[c], maxq = s_maxq[c];
-    const bool finite = s_finite[c] != 0;
-    uint32_t low = 0u, high = 0u;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const uint32_t w = word_of(t.row[i], k >> 1);
-      const uint16_t hb = (k & 1) ? uint16_t(w >> 16) : uint16_t(w & 0xffffu);
-      const uint32_t code = quant_code(h2f(hb), scale, zp, maxq, finite);
-      low |= (code & 3u) << (2 * i);
-      high |= ((code >> 2) & 3u) << (2 * i);
-    }
-    *reinterpret_cast<uint16_t*>(s_low + c * G4 + 2 * tg) = uint16_t(low);
+  // quantise: channel c = 8 cg + k; this thread's 8 tokens -> 16 bits of its low / high rows
+  auto store = [&](int c, uint32_t lo, uint32_t hi) {
+    *reinterpret_cast<uint16_t*>(s_low + low_swz(c, 2 * tg)) = uint16_t(lo);
     const int r = s_row[c];
-    if (r >= 0 && high != 0u) {
+    if (r >= 0 && hi != 0u) {
       const int byte = r * G4 + 2 * tg;   // 2-byte aligned: never straddles a word
-      atomicOr(&s_high[byte >> 2], high << (8 * (byte & 3)));
+      atomicOr(&s_high[byte >> 2], hi << (8 * (byte & 3)));
+    }
+  };
+  const uint16_t* my_src = src + (8 * tg) * a.key_s_tok + 8 * cg;   // this thread's tile (token-major)
+  if (s_nonfinite == 0) {
+    uint32_t mlo = 0u, mhi = 0u;   // near-tie flags: channel k, token i -> bit 8 (k & 3) + i of mlo (k < 4) / mhi
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const int c = 8 * cg + 2 * w;
+      const float2 r = make_float2(s_r[c], s_r[c + 1]);
+      const float2 mz = make_float2(kMagic + s_zp[c], kMagic + s_zp[c + 1]);
+      const float2 top = make_float2(kMagic + s_maxq[c], kMagic + s_maxq[c + 1]);
+      uint32_t ca[8], cb[8];
+      uint32_t& m = (w < 2) ? mlo : mhi;
+      const int kb = 8 * ((2 * w) & 3);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+        fast_pair(word_of(t.row[i], w), r, mz, top, m, 1u << (kb + i), 1u << (kb + 8 + i), ca[i], cb[i]);
+      uint32_t lo_a = pack4(ca[0], ca[1], ca[2], ca[3], 0) | (pack4(ca[4], ca[5], ca[6], ca[7], 0) << 8);
+      uint32_t hi_a = pack4(ca[0], ca[1], ca[2], ca[3], 2) | (pack4(ca[4], ca[5], ca[6], ca[7], 2) << 8);
+      uint32_t lo_b = pack4(cb[0], cb[1], cb[2], cb[3], 0) | (pack4(cb[4], cb[5], cb[6], cb[7], 0) << 8);
+      uint32_t hi_b = pack4(cb[0], cb[1], cb[2], cb[3], 2) | (pack4(cb[4], cb[5], cb[6], cb[7], 2) << 8);
+      const uint32_t fa = (m >> kb) & 0xffu, fb = (m >> (kb + 8)) & 0xffu;
+      if (fa) {
+        const uint2 p = patch_row(fa, my_src + 2 * w, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], lo_a, hi_a);
+        lo_a = p.x; hi_a = p.y;
+      }
+      if (fb) {
+        const uint2 p = patch_row(fb, my_src + 2 * w + 1, a.key_s_tok, s_scale[c + 1], s_zp[c + 1], s_maxq[c + 1], lo_b,
+                                  hi_b);
+        lo_b = p.x; hi_b = p.y;
+      }
+      store(c, lo_a, hi_a);
+      store(c + 1, lo_b, hi_b);
+    }
+  } else {   // non-finite statistics somewhere in the page-head: the exact path throughout
+#pragma unroll 1
+    for (int k = 0; k < 8; ++k) {
+      const int c = 8 * cg + k;
+      const uint2 p = patch_row(0xffu, my_src + k, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], 0u, 0u);
+      store(c, p.x, p.y);
     }
   }
   __syncthreads();
-  uint8_t* out_low = a.key_low + page * a.low_s_page + h * a.low_s_head;
-  reinterpret_cast<uint4*>(out_low)[tid] = reinterpret_cast<const uint4*>(s_low)[tid];
+  {  // row c = tid / 2, bytes 16 (tid & 1) .. +15: four swizzled words
+    const int c = tid >> 1, b0 = 16 * (tid & 1);
+    const uint32_t* srow = reinterpret_cast<const uint32_t*>(s_low);
+    uint4 v;
+    v.x = srow[low_swz(c, b0) >> 2]; v.y = srow[low_swz(c, b0 + 4) >> 2];
+    v.z = srow[low_swz(c, b0 + 8) >> 2]; v.w = srow[low_swz(c, b0 + 12) >> 2];
+    uint8_t* out_low = a.key_low + page * a.low_s_page + h * a.low_s_head;
+    reinterpret_cast<uint4*>(out_low)[tid] = v;
+  }
   uint8_t* out_high = a.key_high + page * a.high_s_page + h * a.high_s_head;
   for (int i = tid; i < K * G4 / 16; i += kFastThreads)
     reinterpret_cast<uint4*>(out_high)[i] = reinterpret_cast<const uint4*>(s_high)[i];
 }
 
-__global__ void __launch_bounds__(kFastThreads)
+__global__ void __launch_bounds__(kFastThreads, 4)
 quantize_value_d128_kernel(const KittyValueQuantArgs a) {
   constexpr int D4 = 32;
   __shared__ __align__(16) uint8_t s_codes[128 * D4];
@@ -394,10 +486,14 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
   load_tile(t, src, a.val_s_tok, tg, cg, n_valid);
   uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.val_scale) + page * a.meta_s_page + h * a.meta_s_head;
   uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.val_zero) + page * a.meta_s_page + h * a.meta_s_head;
+  // per-token min / max over the 16 lanes of the token row; lane cg (< 8) keeps those
+  // of token 8 tg + cg, computes its statistics once, and every lane reads the
+  // statistics of its 8 tokens with shuffles
+  const int mine = cg & 7;
+  float mn_m = 0.0f, mx_m = 0.0f;
+  bool finite = true;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    const int tok = 8 * tg + i;
-    // (min, -max) over this thread's 8 channels, then over the 16 lanes of the token row
     __half2 lo = __hmin2_nan(u2h2(t.row[i].x), u2h2(t.row[i].y));
     __half2 hi = __hmax2_nan(u2h2(t.row[i].x), u2h2(t.row[i].y));
     lo = __hmin2_nan(lo, __hmin2_nan(u2h2(t.row[i].z), u2h2(t.row[i].w)));
@@ -406,24 +502,61 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
                                 __hneg(__hmax_nan(__low2half(hi), __high2half(hi))));
 #pragma unroll
     for (int o = 1; o < 16; o <<= 1) mm = __hmin2_nan(mm, u2h2(__shfl_xor_sync(0xffffffffu, h22u(mm), o)));
-    const float mnf = __low2float(mm), mxf = -__high2float(mm);
-    const float scale = __fdiv_rn(clamp_min(mxf - mnf, 1e-8f), 3.0f);
-    float zp = rintf(__fdiv_rn(-mnf, scale));
-    zp = tmin(tmax(zp, 0.0f), 3.0f);
-    const bool finite = isfinite(mnf) && isfinite(mxf) && isfinite(scale);
-    if (cg == 0) {
-      out_scale[tok * a.meta_s_tok] = f2h(scale);
-      out_zero[tok * a.meta_s_tok] = f2h(zp);
-    }
-    uint32_t bits = 0u;
-#pragma unroll
-    for (int k = 0; k < 8; ++k) {
-      const uint32_t w = word_of(t.row[i], k >> 1);
-      const uint16_t hb = (k & 1) ? uint16_t(w >> 16) : uint16_t(w & 0xffffu);
-      bits |= (quant_code(h2f(hb), scale, zp, 3.0f, finite) & 3u) << (2 * k);
-    }
-    *reinterpret_cast<uint16_t*>(s_codes + tok * D4 + 2 * cg) = uint16_t(bits);
+    const float mn = __low2float(mm), mx = -__high2float(mm);
+    finite = finite && isfinite(mn) && isfinite(mx);
+    mn_m = (mine == i) ? mn : mn_m;
+    mx_m = (mine == i) ? mx : mx_m;
   }
+  const float scale_m = __fdiv_rn(clamp_min(mx_m - mn_m, 1e-8f), 3.0f);
+  const float zp_m = tmin(tmax(rintf(__fdiv_rn(-mn_m, scale_m)), 0.0f), 3.0f);
+  const float rcp_m = __frcp_rn(scale_m);
+  if (cg < 8) {
+    out_scale[(8 * tg + cg) * a.meta_s_tok] = f2h(scale_m);
+    out_zero[(8 * tg + cg) * a.meta_s_tok] = f2h(zp_m);
+  }
+  finite = __all_sync(0xffffffffu, finite);   // warp-uniform: the shuffles below run in every lane
+  const int base_lane = threadIdx.x & 16;
+  uint32_t bits[8];
+  const uint16_t* my_src = src + (8 * tg) * a.val_s_tok + 8 * cg;
+  if (finite) {
+    uint32_t mlo = 0u, mhi = 0u;   // near-tie flags: token i, channel k -> bit 8 (i & 3) + k of mlo (i < 4) / mhi
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float rcp = __shfl_sync(0xffffffffu, rcp_m, base_lane + i);
+      const float zp = __shfl_sync(0xffffffffu, zp_m, base_lane + i);
+      const float2 r2 = make_float2(rcp, rcp);
+      const float2 mz = make_float2(kMagic + zp, kMagic + zp);
+      const float2 top = make_float2(kMagic + 3.0f, kMagic + 3.0f);
+      uint32_t& m = (i < 4) ? mlo : mhi;
+      const int ib = 8 * (i & 3);
+      uint32_t c[8];
+#pragma unroll
+      for (int w = 0; w < 4; ++w)
+        fast_pair(word_of(t.row[i], w), r2, mz, top, m, 1u << (ib + 2 * w), 1u << (ib + 2 * w + 1), c[2 * w],
+                  c[2 * w + 1]);
+      bits[i] = pack4(c[0], c[1], c[2], c[3], 0) | (pack4(c[4], c[5], c[6], c[7], 0) << 8);
+      const uint32_t f = (m >> ib) & 0xffu;
+      const float scale = __shfl_sync(0xffffffffu, scale_m, base_lane + i);
+      if (f && 8 * tg + i < n_valid)
+        bits[i] = patch_row(f, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, bits[i], 0u).x;
+    }
+  } else {   // non-finite statistics in this warp: the exact path (rows beyond n_valid read as zeros)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float scale = __shfl_sync(0xffffffffu, scale_m, base_lane + i);
+      const float zp = __shfl_sync(0xffffffffu, zp_m, base_lane + i);
+      uint32_t b;
+      if (8 * tg + i < n_valid) {
+        b = patch_row(0xffu, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, 0u, 0u).x;
+      } else {
+        b = (quant_code(0.0f, scale, zp, 3.0f) & 3u) * 0x5555u;
+      }
+      bits[i] = b;
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+    *reinterpret_cast<uint16_t*>(s_codes + (8 * tg + i) * D4 + 2 * cg) = uint16_t(bits[i]);
   __syncthreads();
   uint8_t* out = a.val_codes + page * a.codes_s_page + h * a.codes_s_head;
   reinterpret_cast<uint4*>(out)[tid] = reinterpret_cast<const uint4*>(s_codes)[tid];
