@@ -598,12 +598,18 @@ bool mma_supports(const KittyDecodeArgs& a) {
 
 int mma_ctas_per_sm() { return kCtasPerSm; }
 
-// Slots per segment S = num_splits (default kSlotsTarget): every warp takes at least
+// Slots per segment S = num_splits (default kSlotsTarget, more when there are fewer
+// segment items than warps need for a full grid): every warp takes at least
 // F_min = ceil(items_max / S) items, so a segment spans at most ceil(items_max / F_min)
 // + 1 warps, which is the slot count the merge reads.
 void mma_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   const int items_max = a.max_pages_per_seq + 1;
-  int target = a.num_splits > 0 ? a.num_splits : kSlotsTarget;
+  // few segments (small batch, few KV heads per GPU): more slots per segment so that
+  // every warp of the persistent grid gets a slice
+  const int64_t warps = int64_t(sm_count) * kCtasPerSm * kWarps;
+  const int64_t per_warp = std::max<int64_t>(1, int64_t(a.batch) * a.num_kv_heads * items_max / warps);
+  const int auto_target = int(std::max<int64_t>(kSlotsTarget, (items_max + per_warp - 1) / per_warp));
+  int target = a.num_splits > 0 ? a.num_splits : auto_target;
   target = std::max(1, std::min(target, items_max));
   const int f_min = (items_max + target - 1) / target;
   plan->pages_per_split = f_min;
