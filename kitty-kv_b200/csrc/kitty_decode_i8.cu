@@ -315,15 +315,16 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
   return nb;
 }
 
-// fp16 region of (b, h): sinks then tail, 128 tokens per chunk (fp16 MMAs).
-// Token / channel 16 g_ + 2 m + h of the lane <-> row g_ + 8 h of M tile m.
+// Tokens [t_begin, t_end) of the fp16 region of (b, h) (sinks then tail; one chunk
+// item of the segment walk), at most 128 per pass (fp16 MMAs; 16-token tiles without
+// real tokens are skipped).  Scores: token 16 m + g_ + 8 hh <-> row g_ + 8 hh of M tile
+// m; values: channel 16 g_ + 2 m + hh <-> row g_ + 8 hh of M tile m.
 __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, State& st, uint8_t* wsm,
-                                    const Layout& L, float qk_scale, int lane) {
+                                    const Layout& L, float qk_scale, int lane, int t_begin, int t_end) {
   const int g_ = lane >> 2, q_ = lane & 3;
   const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
   const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
-  const int total = sink_len + tail_len;
-  if (total <= 0) return;
+  if (t_end <= t_begin || sink_len + tail_len <= 0) return;
   __half* ph = reinterpret_cast<__half*>(wsm + L.ptab);
   // q of query head g_ >> 1 (B column g_), channels 32 q_ .. 32 q_ + 31: the K
   // index (2q_, 2q_+1, 2q_+8, 2q_+9) of k-step s <-> channel 32 q_ + 4 s + (0..3)
@@ -343,8 +344,9 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
       for (int i = 0; i < 16; ++i) qw[i] = 0u;
     }
   }
-  for (int f0 = 0; f0 < total; f0 += kG) {
-    const int ntok = min(kG, total - f0);
+  for (int f0 = t_begin; f0 < t_end; f0 += kG) {
+    const int ntok = min(kG, t_end - f0);
+    const int tiles = (ntok + 15) >> 4;   // 16-token tiles holding real tokens (warp-uniform)
     auto row = [&](bool key, int t) -> const uint16_t* {   // row of chunk token t (t < ntok)
       const int ft = f0 + t;
       if (ft < sink_len) {
@@ -355,40 +357,45 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
       return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + b * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
                  : reinterpret_cast<const uint16_t*>(a.tail_v) + b * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
     };
+    // scores: tile m rows g_ / g_ + 8 <-> tokens 16 m + g_ / 16 m + g_ + 8 (s[2 m], s[2 m + 1])
     float s[16];
 #pragma unroll
     for (int m = 0; m < 8; ++m) {
-      float acc[4] = {0.f, 0.f, 0.f, 0.f};
-      const int ta = 16 * g_ + 2 * m, tb = ta + 1;
-      uint4 ka[4], kb[4];
+      s[2 * m] = s[2 * m + 1] = -INFINITY;
+      if (m < tiles) {
+        float acc[4] = {0.f, 0.f, 0.f, 0.f};
+        const int ta = 16 * m + g_, tb = ta + 8;
+        uint4 ka[4], kb[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) { ka[i] = make_uint4(0, 0, 0, 0); kb[i] = ka[i]; }
-      if (ta < ntok) {
-        const uint4* r = reinterpret_cast<const uint4*>(row(true, ta) + 32 * q_);
+        for (int i = 0; i < 4; ++i) { ka[i] = make_uint4(0, 0, 0, 0); kb[i] = ka[i]; }
+        if (ta < ntok) {
+          const uint4* r = reinterpret_cast<const uint4*>(row(true, ta) + 32 * q_);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) ka[i] = r[i];
+          for (int i = 0; i < 4; ++i) ka[i] = r[i];
+        }
+        if (tb < ntok) {
+          const uint4* r = reinterpret_cast<const uint4*>(row(true, tb) + 32 * q_);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) kb[i] = r[i];
+        }
+        const uint32_t* wa = reinterpret_cast<const uint32_t*>(ka);
+        const uint32_t* wb = reinterpret_cast<const uint32_t*>(kb);
+#pragma unroll
+        for (int k = 0; k < 8; ++k)
+          mma_f16(acc, wa[2 * k], wb[2 * k], wa[2 * k + 1], wb[2 * k + 1], qw[2 * k], qw[2 * k + 1]);
+        if (ta < ntok) s[2 * m] = acc[0] * qk_scale;
+        if (tb < ntok) s[2 * m + 1] = acc[2] * qk_scale;
       }
-      if (tb < ntok) {
-        const uint4* r = reinterpret_cast<const uint4*>(row(true, tb) + 32 * q_);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) kb[i] = r[i];
-      }
-      const uint32_t* wa = reinterpret_cast<const uint32_t*>(ka);
-      const uint32_t* wb = reinterpret_cast<const uint32_t*>(kb);
-#pragma unroll
-      for (int k = 0; k < 8; ++k) mma_f16(acc, wa[2 * k], wb[2 * k], wa[2 * k + 1], wb[2 * k + 1], qw[2 * k], qw[2 * k + 1]);
-      s[2 * m] = ta < ntok ? acc[0] * qk_scale : -INFINITY;
-      s[2 * m + 1] = tb < ntok ? acc[2] * qk_scale : -INFINITY;
     }
     softmax_step(st, s);
-    // P (scale 1) as fp16 [query head q_][token]
+    // P (scale 1) as fp16 [query head q_][token]; tokens past ntok hold zeros
     {
-      uint32_t w[8];
+      __half* prow = ph + q_ * kPhRow;
 #pragma unroll
-      for (int k = 0; k < 8; ++k) w[k] = pack_f32x2(s[2 * k], s[2 * k + 1]);
-      uint4* dst = reinterpret_cast<uint4*>(ph + q_ * kPhRow + 16 * g_);
-      dst[0] = make_uint4(w[0], w[1], w[2], w[3]);
-      dst[1] = make_uint4(w[4], w[5], w[6], w[7]);
+      for (int m = 0; m < 8; ++m) {
+        prow[16 * m + g_] = __float2half_rn(s[2 * m]);
+        prow[16 * m + g_ + 8] = __float2half_rn(s[2 * m + 1]);
+      }
     }
     __syncwarp();
     // values: M = channels 16 g_ + 2 m (+1), K = tokens 16 k + (2q_, 2q_+1, 2q_+8, 2q_+9)
@@ -397,7 +404,7 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
     for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
     const __half* pb = ph + (g_ >> 1) * kPhRow;
 #pragma unroll 1
-    for (int k = 0; k < 8; ++k) {
+    for (int k = 0; k < tiles; ++k) {
       uint4 v[4][2];
       const int t0 = 16 * k + 2 * q_;
       const int ts[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
@@ -451,15 +458,15 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // ---- this warp's slice of the item space
   const int64_t gw = int64_t(blockIdx.x) * kWarps + warp;
   const int64_t n_warps = int64_t(gridDim.x) * kWarps;
-  SegmentScan sc = scan_segments(a.num_pages, B, H, 0, lane);
+  SegmentScan sc = scan_segments(a, B, H, 0, lane);
   const int64_t total = sc.total;
   int64_t F = (total + n_warps - 1) / n_warps;
   if (F < plan.pages_per_split) F = plan.pages_per_split;
   const int64_t f0 = gw * F;
   if (f0 >= total) return;
   const int64_t f1 = min(total, f0 + F);
-  sc = scan_segments(a.num_pages, B, H, f0, lane);
-  int b = sc.b, h = sc.h, p = sc.p;
+  sc = scan_segments(a, B, H, f0, lane);
+  Cursor pos = make_cursor(a, f0, sc.b, sc.h, sc.p);   // the item being processed
   int slot = int(gw - sc.seg_begin / F);
 
   if (lane == 0) {
@@ -479,9 +486,10 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   uint32_t k_phase = 0, v_phase = 0;
   bool failed = false;
 
-  auto phys = [&](int bb, int pp) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - 1)]; };
+  // physical page of page item p (>= n16) of sequence bb
+  auto phys = [&](int bb, int pp, int n16) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - n16)]; };
   auto issue_k = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p);
+    int64_t page = phys(c.b, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_k, k_tx);
@@ -490,7 +498,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
   };
   auto issue_v = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p);
+    int64_t page = phys(c.b, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_v, v_tx);
@@ -498,15 +506,15 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     bulk_g2s(smem_u32(vbuf + 4096), reinterpret_cast<const uint8_t*>(a.val_meta) + phh * (2 * kG * 2), 512u, bar_v);
   };
 
-  Cursor cur{f0, b, h, p};
-  bool have_next = cursor_to_page(cur, a.num_pages, H, f1);
+  Cursor cur = pos;
+  bool have_next = cursor_to_page(cur, a, f1);
   if (lane == 0 && have_next) { issue_k(cur); issue_v(cur); }
   __syncwarp();
 
   State st;
   reset_state(st);
   uint32_t qreg[8];
-  int nb = setup_segment(a, b, h, g, wsm, L, lane, qreg);
+  int nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane, qreg);
 
   // B operand bases: column g_ of an MMA = query head g_ >> 1, digit (g_ & 1 ? lo : hi)
   const uint8_t* kb1 = dtab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;   // b1 | b0
@@ -514,10 +522,13 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   const uint8_t* vb = ptab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;    // y1 | y0
 
   for (int64_t f = f0; f < f1; ++f) {
-    if (p == 0) {
-      process_fp16_region(a, b, h, g, st, wsm, L, qk_scale, lane);
+    const int b = pos.b, h = pos.h;
+    if (pos.p < pos.n16) {
+      int t0, t1;
+      fp16_chunk(fp16_tokens(a, b), pos.n16, pos.p, t0, t1);
+      process_fp16_region(a, b, h, g, st, wsm, L, qk_scale, lane, t0, t1);
     } else {
-      const int64_t page = phys(b, p);
+      const int64_t page = phys(b, pos.p, pos.n16);
       const bool valid = page >= 0 && page < a.pool_pages;
       if (!mbar_wait(bar_k, k_phase)) { failed = true; break; }
       k_phase ^= 1u;
@@ -607,8 +618,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       }
       __syncwarp();
       // keys consumed: request the next page's keys
-      cursor_step(cur, a.num_pages, H);
-      have_next = cursor_to_page(cur, a.num_pages, H, f1);
+      have_next = cursor_step(cur, a) && cursor_to_page(cur, a, f1);
       if (lane == 0 && have_next) issue_k(cur);
 
       // ---- scores (log2 domain) of tokens 16 g_ + v, v = 2 m + hh
@@ -698,8 +708,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     }
 
     // ---- advance; write the partial at a segment end or at the end of the slice
-    ++p;
-    const bool seg_end = p >= a.num_pages[b] + 1;
+    const bool seg_end = pos.p + 1 >= pos.items;
     if (seg_end || f + 1 == f1) {
       float l = st.l, zs = st.zs;
       l += __shfl_xor_sync(0xffffffffu, l, 4);
@@ -721,12 +730,13 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       }
       if (seg_end && lane == 0) plan.ws_count[int64_t(b) * H + h] = slot + 1;
       reset_state(st);
-      if (seg_end && f + 1 < f1) {
-        p = 0;
-        if (++h == H) { h = 0; ++b; }
+    }
+    if (f + 1 < f1) {
+      cursor_step(pos, a);
+      if (seg_end) {
         slot = 0;
         __syncwarp();
-        nb = setup_segment(a, b, h, g, wsm, L, lane, qreg);
+        nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane, qreg);
       }
     }
   }
@@ -760,7 +770,7 @@ int i8_ctas_per_sm() { return kCtasPerSm; }
 
 // Same slicing rule as the fp16 tensor-core variant (see mma_plan).
 void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
-  const int items_max = a.max_pages_per_seq + 1;
+  const int items_max = a.max_pages_per_seq + dev::kMaxFp16Items;   // pages + fp16 chunk items
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
   const int64_t warps = int64_t(sm_count) * kCtasPerSm * kWarps;

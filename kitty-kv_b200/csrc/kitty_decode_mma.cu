@@ -259,15 +259,15 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
 // fp16 region of (b, h): sinks then tail, 128 tokens per chunk, read straight
 // from global memory with 16-byte loads.
 __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, WarpState& st, uint8_t* wsm,
-                                    const WarpLayout& L, float qk_scale, int lane) {
+                                    const WarpLayout& L, float qk_scale, int lane, int t_begin, int t_end) {
   const int g_ = lane >> 2, q_ = lane & 3;
   const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
   const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
-  const int total = sink_len + tail_len;
+  (void)tail_len;
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(wsm + L.qnat);   // [8][64] words
   __half* ps = reinterpret_cast<__half*>(wsm + L.ps);
-  for (int f0 = 0; f0 < total; f0 += kG) {
-    const int ntok = min(kG, total - f0);
+  for (int f0 = t_begin; f0 < t_end; f0 += kG) {
+    const int ntok = min(kG, t_end - f0);
     auto row = [&](bool key, int t) -> const uint16_t* {   // row of chunk token t (t < ntok)
       const int ft = f0 + t;
       if (ft < sink_len) {
@@ -367,15 +367,15 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // ---- this warp's slice of the item space
   const int64_t gw = int64_t(blockIdx.x) * kWarps + warp;
   const int64_t n_warps = int64_t(gridDim.x) * kWarps;
-  SegmentScan sc = scan_segments(a.num_pages, B, H, 0, lane);
+  SegmentScan sc = scan_segments(a, B, H, 0, lane);
   const int64_t total = sc.total;
   int64_t F = (total + n_warps - 1) / n_warps;
   if (F < plan.pages_per_split) F = plan.pages_per_split;
   const int64_t f0 = gw * F;
   if (f0 >= total) return;
   const int64_t f1 = min(total, f0 + F);
-  sc = scan_segments(a.num_pages, B, H, f0, lane);
-  int b = sc.b, h = sc.h, p = sc.p;
+  sc = scan_segments(a, B, H, f0, lane);
+  Cursor pos = make_cursor(a, f0, sc.b, sc.h, sc.p);   // the item being processed
   int slot = int(gw - sc.seg_begin / F);
 
   if (lane == 0) {
@@ -392,10 +392,10 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   uint32_t k_phase = 0, v_phase = 0;
   bool failed = false;
 
-  // physical page of item (bb, pp >= 1); out-of-range entries fetch page 0 and are skipped
-  auto phys = [&](int bb, int pp) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - 1)]; };
+  // physical page of page item pp (>= n16) of sequence bb; out-of-range entries fetch page 0 and are skipped
+  auto phys = [&](int bb, int pp, int n16) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - n16)]; };
   auto issue_k = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p);
+    int64_t page = phys(c.b, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_k, k_tx);
@@ -404,7 +404,7 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
   };
   auto issue_v = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p);
+    int64_t page = phys(c.b, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_v, v_tx);
@@ -412,21 +412,24 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     bulk_g2s(smem_u32(vbuf + 4096), reinterpret_cast<const uint8_t*>(a.val_meta) + phh * (2 * kG * 2), 512u, bar_v);
   };
 
-  Cursor cur{f0, b, h, p};
-  bool have_next = cursor_to_page(cur, a.num_pages, H, f1);
+  Cursor cur = pos;
+  bool have_next = cursor_to_page(cur, a, f1);
   if (lane == 0 && have_next) { issue_k(cur); issue_v(cur); }
   __syncwarp();
 
   WarpState st;
   reset_state(st);
-  int nb = setup_segment(a, b, h, g, wsm, L, lane);
+  int nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane);
 
   for (int64_t f = f0; f < f1; ++f) {
-    if (p == 0) {
-      process_fp16_region(a, b, h, st, wsm, L, qk_scale, lane);
+    const int b = pos.b, h = pos.h;
+    if (pos.p < pos.n16) {
+      int t0, t1;
+      fp16_chunk(fp16_tokens(a, b), pos.n16, pos.p, t0, t1);
+      process_fp16_region(a, b, h, st, wsm, L, qk_scale, lane, t0, t1);
     } else {
       // this page is the producer cursor's current page
-      const int64_t page = phys(b, p);
+      const int64_t page = phys(b, pos.p, pos.n16);
       const bool valid = page >= 0 && page < a.pool_pages;
       if (!mbar_wait(bar_k, k_phase)) { failed = true; break; }
       k_phase ^= 1u;
@@ -480,8 +483,7 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       }
       __syncwarp();
       // keys consumed: request the next page's keys
-      cursor_step(cur, a.num_pages, H);
-      have_next = cursor_to_page(cur, a.num_pages, H, f1);
+      have_next = cursor_step(cur, a) && cursor_to_page(cur, a, f1);
       if (lane == 0 && have_next) issue_k(cur);
 
       const float zk0 = __shfl_sync(0xffffffffu, zk[0], q_);
@@ -528,8 +530,7 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     }
 
     // ---- advance; write the partial at a segment end or at the end of the slice
-    ++p;
-    const bool seg_end = p >= a.num_pages[b] + 1;
+    const bool seg_end = pos.p + 1 >= pos.items;
     if (seg_end || f + 1 == f1) {
       float l0 = st.l[0], l1 = st.l[1];
 #pragma unroll
@@ -561,12 +562,13 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       }
       if (seg_end && lane == 0) plan.ws_count[int64_t(b) * H + h] = slot + 1;
       reset_state(st);
-      if (seg_end && f + 1 < f1) {
-        p = 0;
-        if (++h == H) { h = 0; ++b; }
+    }
+    if (f + 1 < f1) {
+      cursor_step(pos, a);
+      if (seg_end) {
         slot = 0;
         __syncwarp();
-        nb = setup_segment(a, b, h, g, wsm, L, lane);
+        nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane);
       }
     }
   }
@@ -603,7 +605,7 @@ int mma_ctas_per_sm() { return kCtasPerSm; }
 // F_min = ceil(items_max / S) items, so a segment spans at most ceil(items_max / F_min)
 // + 1 warps, which is the slot count the merge reads.
 void mma_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
-  const int items_max = a.max_pages_per_seq + 1;
+  const int items_max = a.max_pages_per_seq + dev::kMaxFp16Items;   // pages + fp16 chunk items
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
   const int64_t warps = int64_t(sm_count) * kCtasPerSm * kWarps;

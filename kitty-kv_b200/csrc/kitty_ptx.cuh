@@ -91,8 +91,32 @@ __device__ __forceinline__ uint32_t pack16(uint32_t lo, uint32_t hi) { return lo
 
 // ---- segment walk -----------------------------------------------------------
 //
-// Segment (b, h) has L_b = num_pages[b] + 1 items: item 0 is the fp16 region
-// (sinks then tail), items 1..n are the quantised pages in block-table order.
+// Segment (b, h) has L_b = n16_b + num_pages[b] items: items 0 .. n16_b - 1 are
+// chunks of its fp16 region (sinks then tail, at most kMaxFp16Items chunks of
+// about the same length, at least one item even when the region is empty), items
+// n16_b .. are the quantised pages in block-table order.  Splitting the fp16 region
+// lets several warps share it.
+
+constexpr int kFp16ChunkTokens = 32;   // a chunk item covers at least this many tokens
+constexpr int kMaxFp16Items = 4;
+
+__device__ __forceinline__ int fp16_tokens(const KittyDecodeArgs& a, int b) {
+  return max(a.sink_len ? a.sink_len[b] : a.sink_len_all, 0) + max(a.tail_len ? a.tail_len[b] : a.tail_len_all, 0);
+}
+__device__ __forceinline__ int fp16_items(int tokens) {
+  return tokens <= kFp16ChunkTokens ? 1 : min(kMaxFp16Items, (tokens + kFp16ChunkTokens - 1) / kFp16ChunkTokens);
+}
+// items of the segments of sequence b; n16 receives its fp16 items
+__device__ __forceinline__ int seg_items(const KittyDecodeArgs& a, int b, int& n16) {
+  n16 = fp16_items(fp16_tokens(a, b));
+  return n16 + max(a.num_pages[b], 0);
+}
+// tokens [t0, t1) of fp16 chunk c of a region of `tokens` tokens split into n16 chunks
+__device__ __forceinline__ void fp16_chunk(int tokens, int n16, int c, int& t0, int& t1) {
+  const int len = (tokens + n16 - 1) / n16;
+  t0 = min(tokens, c * len);
+  t1 = min(tokens, t0 + len);
+}
 
 struct SegmentScan {
   int64_t total;     // items over all segments
@@ -101,15 +125,16 @@ struct SegmentScan {
 };
 
 // Warp-cooperative: total item count and the (b, h, p) of item f (when f < total).
-// Segment (b, h) has L_b = num_pages[b] + 1 items; sequence b's segments start at
-// H * sum_{b' < b} L_b'.
-__device__ inline SegmentScan scan_segments(const int32_t* num_pages, int B, int H, int64_t f, int lane) {
+// Sequence b's segments start at H * sum_{b' < b} L_b'.
+__device__ inline SegmentScan scan_segments(const KittyDecodeArgs& a, int B, int H, int64_t f, int lane) {
   SegmentScan r;
   r.b = -1; r.h = 0; r.p = 0; r.seg_begin = 0;
   int64_t run = 0;
   for (int b0 = 0; b0 < B; b0 += 32) {
     const int b = b0 + lane;
-    const int64_t seq_items = (b < B) ? int64_t(H) * (int64_t(max(num_pages[b], 0)) + 1) : 0;
+    int n16 = 0;
+    const int64_t L = (b < B) ? seg_items(a, b, n16) : 0;
+    const int64_t seq_items = int64_t(H) * L;
     int64_t incl = seq_items;
 #pragma unroll
     for (int o = 1; o < 32; o <<= 1) {
@@ -122,12 +147,11 @@ __device__ inline SegmentScan scan_segments(const int32_t* num_pages, int B, int
     if (bal != 0u && r.b < 0) {
       const int src = __ffs(bal) - 1;
       const int64_t st = __shfl_sync(0xffffffffu, start, src);
-      const int bb = b0 + src;
-      const int64_t L = int64_t(max(num_pages[bb], 0)) + 1;
-      r.b = bb;
-      r.h = int((f - st) / L);
-      r.p = int((f - st) - int64_t(r.h) * L);
-      r.seg_begin = st + int64_t(r.h) * L;
+      const int64_t Ls = __shfl_sync(0xffffffffu, L, src);
+      r.b = b0 + src;
+      r.h = int((f - st) / Ls);
+      r.p = int((f - st) - int64_t(r.h) * Ls);
+      r.seg_begin = st + int64_t(r.h) * Ls;
     }
     run += __shfl_sync(0xffffffffu, incl, 31);
   }
@@ -135,22 +159,40 @@ __device__ inline SegmentScan scan_segments(const int32_t* num_pages, int B, int
   return r;
 }
 
-// Producer cursor over the real pages of a warp's slice.
+// Walk over a warp's slice (items, segments); used for the consumer position and for
+// the producer cursor that runs ahead over the real pages.
 struct Cursor {
-  int64_t f;   // item index
-  int b, h, p; // sequence, KV head, item in segment (p >= 1: page p - 1)
+  int64_t f;      // item index
+  int b, h, p;    // sequence, KV head, item in segment
+  int n16, items; // fp16 items and all items of the current segment
 };
 
-__device__ __forceinline__ void cursor_step(Cursor& c, const int32_t* num_pages, int H) {
+__device__ __forceinline__ Cursor make_cursor(const KittyDecodeArgs& a, int64_t f, int b, int h, int p) {
+  Cursor c;
+  c.f = f; c.b = b; c.h = h; c.p = p;
+  c.items = seg_items(a, b, c.n16);
+  return c;
+}
+
+// next item; false past the last segment
+__device__ __forceinline__ bool cursor_step(Cursor& c, const KittyDecodeArgs& a) {
   ++c.f; ++c.p;
-  if (c.p >= num_pages[c.b] + 1) { c.p = 0; if (++c.h == H) { c.h = 0; ++c.b; } }
+  if (c.p >= c.items) {
+    c.p = 0;
+    if (++c.h == a.num_kv_heads) {
+      c.h = 0;
+      if (++c.b >= a.batch) return false;
+    }
+    c.items = seg_items(a, c.b, c.n16);
+  }
+  return true;
 }
 
 // advance to the next real page in [c.f, end); false if none
-__device__ __forceinline__ bool cursor_to_page(Cursor& c, const int32_t* num_pages, int H, int64_t end) {
+__device__ __forceinline__ bool cursor_to_page(Cursor& c, const KittyDecodeArgs& a, int64_t end) {
   while (c.f < end) {
-    if (c.p >= 1) return true;
-    cursor_step(c, num_pages, H);
+    if (c.p >= c.n16) return true;
+    if (!cursor_step(c, a)) return false;
   }
   return false;
 }
