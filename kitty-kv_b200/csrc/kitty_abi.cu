@@ -88,7 +88,7 @@ void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
     const int64_t target = int64_t(device_sm_count()) * ctas_per_sm * 2;
     splits = int(std::max<int64_t>(1, (target + units - 1) / std::max<int64_t>(units, 1)));
   }
-  splits = std::max(1, std::min(splits, std::max(1, maxp)));
+  splits = std::max(1, std::min({splits, std::max(1, maxp), kMaxDecodeSlots}));
   const int pps = maxp > 0 ? (maxp + splits - 1) / splits : 1;
   plan->pages_per_split = pps;
   plan->num_splits = maxp > 0 ? (maxp + pps - 1) / pps : 1;

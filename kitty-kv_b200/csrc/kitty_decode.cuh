@@ -28,6 +28,9 @@ struct DecodePlan {
   int* ws_count;      // [B][H] slots written (tensor-core variant), else nullptr
 };
 
+// Most partial slots the merge kernel combines per (sequence, KV head).
+constexpr int kMaxDecodeSlots = 1024;
+
 int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 int launch_decode_mma(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);

@@ -612,7 +612,7 @@ void mma_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   const int64_t per_warp = std::max<int64_t>(1, int64_t(a.batch) * a.num_kv_heads * items_max / warps);
   const int auto_target = int(std::max<int64_t>(kSlotsTarget, (items_max + per_warp - 1) / per_warp));
   int target = a.num_splits > 0 ? a.num_splits : auto_target;
-  target = std::max(1, std::min(target, items_max));
+  target = std::max(1, std::min({target, items_max, kMaxDecodeSlots - 1}));
   const int f_min = (items_max + target - 1) / target;
   plan->pages_per_split = f_min;
   plan->num_splits = (items_max + f_min - 1) / f_min + 1;

@@ -258,27 +258,73 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 }  // namespace
 
 // Merge the per-split partials: out = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s.
-__global__ void decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+// Combines the split partials of one (sequence, query head): max M over the slots,
+// weights w_s = exp(m_s - M), L = sum_s w_s l_s, out = sum_s w_s o_s / L.  The slot
+// weights are computed once (one lane per slot) and kept in shared memory, and the
+// accumulation over slots issues its loads in groups of eight, so a call with many
+// slots costs a few memory latencies instead of one per slot.
+constexpr int kMergeThreads = 128;
+constexpr int kMergeMaxSlots = kMaxDecodeSlots;
+
+__global__ void __launch_bounds__(kMergeThreads)
+decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+  __shared__ float s_w[kMergeMaxSlots];
+  __shared__ float s_red[kMergeThreads / 32];
+  __shared__ float s_M, s_L;
   const int b = blockIdx.y, qhg = blockIdx.x;  // global query head
   const int H = a.num_kv_heads, g = a.num_q_heads / H, D = a.head_dim;
   const int h = qhg / g, qh = qhg - h * g;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t base = (int64_t(b) * H + h) * plan.num_splits;
   // slots written for this (sequence, head): all of them, or the recorded count
-  const int nsl = plan.ws_count ? min(max(plan.ws_count[int64_t(b) * H + h], 0), plan.num_splits) : plan.num_splits;
-  float M = -INFINITY;
-  for (int s = 0; s < nsl; ++s) M = fmaxf(M, plan.ws_m[(base + s) * g + qh]);
-  float L = 0.f;
-  for (int s = 0; s < nsl; ++s) {
-    const float m = plan.ws_m[(base + s) * g + qh];
-    if (m != -INFINITY) L += __expf(m - M) * plan.ws_l[(base + s) * g + qh];
+  const int nsl = min(plan.ws_count ? min(max(plan.ws_count[int64_t(b) * H + h], 0), plan.num_splits)
+                                    : plan.num_splits, kMergeMaxSlots);
+  float mx = -INFINITY;
+  for (int s = tid; s < nsl; s += kMergeThreads) mx = fmaxf(mx, plan.ws_m[(base + s) * g + qh]);
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+  if (lane == 0) s_red[warp] = mx;
+  __syncthreads();
+  if (tid == 0) {
+    float M = s_red[0];
+    for (int w = 1; w < kMergeThreads / 32; ++w) M = fmaxf(M, s_red[w]);
+    s_M = M;
   }
+  __syncthreads();
+  const float M = s_M;
+  float part = 0.f;
+  for (int s = tid; s < nsl; s += kMergeThreads) {
+    const float m = plan.ws_m[(base + s) * g + qh];
+    const float w = (m == -INFINITY) ? 0.f : __expf(m - M);
+    s_w[s] = w;
+    part += w * plan.ws_l[(base + s) * g + qh];
+  }
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) part += __shfl_xor_sync(0xffffffffu, part, o);
+  __syncthreads();
+  if (lane == 0) s_red[warp] = part;
+  __syncthreads();
+  if (tid == 0) {
+    float L = 0.f;
+    for (int w = 0; w < kMergeThreads / 32; ++w) L += s_red[w];
+    s_L = L;
+  }
+  __syncthreads();
+  const float L = s_L;
   uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + qhg * a.out_s_head;
-  for (int c = threadIdx.x; c < D; c += blockDim.x) {
+  const float* o = plan.ws_o + ((base) * g + qh) * int64_t(D);
+  const int64_t slot_stride = int64_t(g) * D;
+  for (int c = tid; c < D; c += kMergeThreads) {
     float acc = 0.f;
-    for (int s = 0; s < nsl; ++s) {
-      const float m = plan.ws_m[(base + s) * g + qh];
-      if (m != -INFINITY) acc += __expf(m - M) * plan.ws_o[((base + s) * g + qh) * D + c];
+    int s = 0;
+    for (; s + 8 <= nsl; s += 8) {
+      float v[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) v[k] = o[(s + k) * slot_stride + c];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) acc += s_w[s + k] * v[k];
     }
+    for (; s < nsl; ++s) acc += s_w[s] * o[s * slot_stride + c];
     out[c] = f2h(L > 0.f ? acc / L : 0.f);
   }
 }
@@ -296,7 +342,9 @@ int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStr
 
 int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
   dim3 grid(a.num_q_heads, a.batch);
-  decode_merge_kernel<<<grid, 128, 0, stream>>>(a, plan);
+  if (plan.num_splits > kMergeMaxSlots)
+    return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: more than 1024 partial slots per sequence and head");
+  decode_merge_kernel<<<grid, kMergeThreads, 0, stream>>>(a, plan);
   return check_launch("decode_merge_kernel");
 }
 
