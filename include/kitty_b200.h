@@ -37,7 +37,7 @@ extern "C" {
 #define KITTY_ERR_CUDA 3             /* a CUDA runtime call failed */
 #define KITTY_ERR_WORKSPACE 4        /* workspace missing or too small */
 
-#define KITTY_ABI_VERSION 1
+#define KITTY_ABI_VERSION 2
 
 /* ABI version compiled into the library (KITTY_ABI_VERSION). */
 int kitty_abi_version(void);
@@ -47,7 +47,8 @@ const char* kitty_last_error(void);
 
 /* sizeof() of the argument structs below, so a foreign-function binding can
  * check its mirror of them: kind 0 = KittyKeyQuantArgs, 1 = KittyValueQuantArgs,
- * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs; 0 for an unknown kind. */
+ * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs, 4 = KittyCacheState; 0 for an
+ * unknown kind. */
 size_t kitty_args_size(int kind);
 
 /* ---------------------------------------------------------------------------
@@ -66,7 +67,8 @@ size_t kitty_args_size(int kind);
  * Job j, head h: the source element (token t, channel c) is at
  *   key + key_off[j] + h*key_s_head + t*key_s_tok + c*key_s_ch   (fp16 elements)
  * and the outputs go to page-head (dst_page[j], h) of the pools, whose page /
- * head strides are given in elements (the slice itself is contiguous).
+ * head strides are given in elements (the slice itself is contiguous).  Jobs
+ * with dst_page[j] < 0 are skipped (same for the value quantiser).
  * ------------------------------------------------------------------------- */
 typedef struct KittyKeyQuantArgs {
   const void* key;            /* fp16 source */
@@ -191,6 +193,11 @@ typedef struct KittyDecodeArgs {
   int32_t num_splits;                 /* 0 = choose */
   void* workspace;
   size_t workspace_bytes;
+  /* Row b of q / out reads the cache row seq_map[b] of num_pages, sink_len,
+   * tail_len, block_table and the sink / tail tensors (for a decode over a
+   * subset of a KittyCacheState's sequences, in any order).  NULL = b.  Values
+   * must be valid rows of those arrays. */
+  const int32_t* seq_map;
 } KittyDecodeArgs;
 
 /* Bytes of workspace kitty_paged_decode needs; writes the split count it will
@@ -211,10 +218,96 @@ int kitty_paged_decode(const KittyDecodeArgs* args, void* stream);
  * does not fit returns KITTY_ERR_WORKSPACE.  Allocates nothing. */
 int kitty_paged_decode_noalloc(const KittyDecodeArgs* args, void* stream);
 
+/* ---------------------------------------------------------------------------
+ * Device-resident cache state: per-sequence fp16 buffers, counters, block
+ * tables and a free-page stack, all in device memory, so that a decode step of
+ * many sequences appends its tokens (and flushes the buffers that fill into
+ * new pages) without a host round trip.
+ *
+ * Replaces, for one layer and a batch of sequences at once,
+ * KittyInferencePipeline.push_token / _trigger_quantization / reset_sequence
+ * (kitty/pipeline.py:115-181, 183-258, 286-313) and the page allocator of
+ * PageCentricKVLayoutManager (allocate_page / free_sequence,
+ * kitty/layout.py:161-220).  Same state machine per sequence: the first S
+ * tokens go to the fp16 sinks, later tokens to a G-token fp16 buffer; when
+ * that buffer fills, its keys and values are quantised into a newly allocated
+ * page (the values of the same G tokens, like the pipeline's aligned-values
+ * mode; the reference's separate value window is not kept here).
+ *
+ * Arrays (all device memory, contiguous):
+ *   sink_k, sink_v   fp16 [max_seqs][H][S][D]
+ *   tail_k, tail_v   fp16 [max_seqs][H][G][D]
+ *   sink_len, tail_len, num_pages, claim   int32 [max_seqs]
+ *   block_table      int32 [max_seqs][max_pages_per_seq]
+ *   free_pages       int32 [pool_pages]  (stack: entries [0, *free_top))
+ *   free_top         int32 [1]
+ *   job_off int64, job_page int32, job_slot int32   [max_seqs] scratch
+ *   pools            the page layout at the top of this file, P = pool_pages
+ * Several states (one per layer) may share the pools, free_pages and free_top;
+ * their launches must then be ordered (one stream).  The state can be passed
+ * straight to kitty_paged_decode: block_table / num_pages / sink_len /
+ * tail_len / sink_* / tail_* with row strides of the layouts above, and
+ * seq_map = the step's sequence ids.
+ * ------------------------------------------------------------------------- */
+typedef struct KittyCacheState {
+  int32_t max_seqs, num_heads, head_dim, group, sink_size, d_boost, sentinel;
+  int32_t max_pages_per_seq;
+  int64_t pool_pages;
+  const uint8_t* boost_idx;           /* [H][D] */
+  int64_t bidx_s_head;
+  void* sink_k;
+  void* sink_v;
+  void* tail_k;
+  void* tail_v;
+  int32_t* sink_len;
+  int32_t* tail_len;
+  int32_t* num_pages;
+  int32_t* claim;                     /* zero between calls */
+  int32_t* block_table;
+  int32_t* free_pages;
+  int32_t* free_top;
+  uint8_t* key_low;
+  uint8_t* key_high;
+  void* key_meta;
+  uint8_t* val_codes;
+  void* val_meta;
+  int64_t* job_off;
+  int32_t* job_page;
+  int32_t* job_slot;
+} KittyCacheState;
+
+/* Empty every sequence and put all pool pages on the free stack (pages are
+ * handed out in increasing order until some are released).  Use it once on a
+ * new state; states sharing a stack need it once. */
+int kitty_cache_reset(const KittyCacheState* state, void* stream);
+
+/* Append one token to each of n distinct sequences: seq_ids[i] (device memory)
+ * receives key / value row i, fp16, element (i, h, c) at
+ * key + i*k_s_tok + h*k_s_head + c (16-byte aligned rows: pointer and strides
+ * multiples of 8 elements).  A sequence whose G-token buffer fills is flushed
+ * in the same call: a page is popped from the free stack, appended to its
+ * block table, and the buffer quantised into it (bit-exact with
+ * kitty_quantize_key_pages / kitty_quantize_value_pages on the same tokens).
+ * Four launches on `stream` (plan, copy, key and value quantisation), no host
+ * synchronisation, n <= max_seqs.  Failures found on the device drop that
+ * token, leave its sequence unchanged and set a sticky error bit
+ * (kitty_device_error_flags): bit 1 no free page, bit 2 block table full,
+ * bit 3 sequence id out of range or repeated in the batch. */
+int kitty_cache_append(const KittyCacheState* state, int32_t n, const int32_t* seq_ids,
+                       const void* key, int64_t k_s_tok, int64_t k_s_head,
+                       const void* value, int64_t v_s_tok, int64_t v_s_head, void* stream);
+
+/* Empty the n sequences seq_ids[i] (device memory) and push their pages back on
+ * the free stack (in block-table order, sequence after sequence).  Releasing an
+ * empty sequence is a no-op; ids out of range set error bit 3; a stack that
+ * would overflow pool_pages sets bit 4 and keeps the pages of that sequence. */
+int kitty_cache_release(const KittyCacheState* state, int32_t n, const int32_t* seq_ids, void* stream);
+
 /* Sticky error bits set by device code on the current device (bit 0: a decode
  * kernel gave up waiting for a bulk copy after its bounded wait and returned
- * without a valid result).  Synchronises with the device; clear != 0 resets the
- * bits after reading them. */
+ * without a valid result; bits 1-4: kitty_cache_append / kitty_cache_release,
+ * above).  Synchronises with the device; clear != 0 resets the bits after
+ * reading them. */
 int kitty_device_error_flags(uint32_t* flags, int clear);
 
 /* Test and benchmark hook, no counterpart in the reference: pin the decode

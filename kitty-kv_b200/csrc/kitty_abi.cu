@@ -11,6 +11,7 @@ namespace kitty {
 int quantize_key_pages_impl(const KittyKeyQuantArgs* a, void* stream);
 int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream);
 int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream);
+int read_cache_error(uint32_t* flags, int clear);
 
 namespace {
 thread_local std::string g_last_error;
@@ -126,6 +127,7 @@ size_t kitty_args_size(int kind) {
     case 1: return sizeof(KittyValueQuantArgs);
     case 2: return sizeof(KittyKeyDequantArgs);
     case 3: return sizeof(KittyDecodeArgs);
+    case 4: return sizeof(KittyCacheState);
     default: return 0;
   }
 }
@@ -148,12 +150,14 @@ int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream) {
 int kitty_device_error_flags(uint32_t* flags, int clear) {
   clear_error();
   if (!flags) return fail(KITTY_ERR_INVALID_ARGUMENT, "device_error_flags: flags is NULL");
-  uint32_t a = 0, b = 0;
+  uint32_t a = 0, b = 0, c = 0;
   int rc = read_decode_error(&a, clear);
   if (rc != KITTY_OK) return rc;
   rc = read_decode_error_i8(&b, clear);
   if (rc != KITTY_OK) return rc;
-  *flags = a | b;
+  rc = read_cache_error(&c, clear);
+  if (rc != KITTY_OK) return rc;
+  *flags = a | b | c;
   return KITTY_OK;
 }
 

@@ -321,9 +321,10 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
 // m; values: channel 16 g_ + 2 m + hh <-> row g_ + 8 hh of M tile m.
 __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, State& st, uint8_t* wsm,
                                     const Layout& L, float qk_scale, int lane, int t_begin, int t_end) {
+  const int cr = cache_row(a, b);   // cache row (sinks, tail, lengths)
   const int g_ = lane >> 2, q_ = lane & 3;
-  const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
-  const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
+  const int sink_len = a.sink_len ? a.sink_len[cr] : a.sink_len_all;
+  const int tail_len = a.tail_len ? a.tail_len[cr] : a.tail_len_all;
   if (t_end <= t_begin || sink_len + tail_len <= 0) return;
   __half* ph = reinterpret_cast<__half*>(wsm + L.ptab);
   // q of query head g_ >> 1 (B column g_), channels 32 q_ .. 32 q_ + 31: the K
@@ -350,12 +351,12 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
     auto row = [&](bool key, int t) -> const uint16_t* {   // row of chunk token t (t < ntok)
       const int ft = f0 + t;
       if (ft < sink_len) {
-        return key ? reinterpret_cast<const uint16_t*>(a.sink_k) + b * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
-                   : reinterpret_cast<const uint16_t*>(a.sink_v) + b * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok;
+        return key ? reinterpret_cast<const uint16_t*>(a.sink_k) + cr * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
+                   : reinterpret_cast<const uint16_t*>(a.sink_v) + cr * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok;
       }
       const int tt = ft - sink_len;
-      return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + b * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
-                 : reinterpret_cast<const uint16_t*>(a.tail_v) + b * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
+      return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + cr * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
+                 : reinterpret_cast<const uint16_t*>(a.tail_v) + cr * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
     };
     // scores: tile m rows g_ / g_ + 8 <-> tokens 16 m + g_ / 16 m + g_ + 8 (s[2 m], s[2 m + 1])
     float s[16];
@@ -489,7 +490,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // physical page of page item p (>= n16) of sequence bb
   auto phys = [&](int bb, int pp, int n16) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - n16)]; };
   auto issue_k = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p, c.n16);
+    int64_t page = phys(c.s, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_k, k_tx);
@@ -498,7 +499,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
   };
   auto issue_v = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p, c.n16);
+    int64_t page = phys(c.s, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_v, v_tx);
@@ -525,10 +526,10 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     const int b = pos.b, h = pos.h;
     if (pos.p < pos.n16) {
       int t0, t1;
-      fp16_chunk(fp16_tokens(a, b), pos.n16, pos.p, t0, t1);
+      fp16_chunk(fp16_tokens(a, pos.s), pos.n16, pos.p, t0, t1);
       process_fp16_region(a, b, h, g, st, wsm, L, qk_scale, lane, t0, t1);
     } else {
-      const int64_t page = phys(b, pos.p, pos.n16);
+      const int64_t page = phys(pos.s, pos.p, pos.n16);
       const bool valid = page >= 0 && page < a.pool_pages;
       if (!mbar_wait(bar_k, k_phase)) { failed = true; break; }
       k_phase ^= 1u;

@@ -260,9 +260,10 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
 // from global memory with 16-byte loads.
 __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, WarpState& st, uint8_t* wsm,
                                     const WarpLayout& L, float qk_scale, int lane, int t_begin, int t_end) {
+  const int cr = cache_row(a, b);   // cache row (sinks, tail, lengths)
   const int g_ = lane >> 2, q_ = lane & 3;
-  const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
-  const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
+  const int sink_len = a.sink_len ? a.sink_len[cr] : a.sink_len_all;
+  const int tail_len = a.tail_len ? a.tail_len[cr] : a.tail_len_all;
   (void)tail_len;
   const uint32_t* qw = reinterpret_cast<const uint32_t*>(wsm + L.qnat);   // [8][64] words
   __half* ps = reinterpret_cast<__half*>(wsm + L.ps);
@@ -271,12 +272,12 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, Warp
     auto row = [&](bool key, int t) -> const uint16_t* {   // row of chunk token t (t < ntok)
       const int ft = f0 + t;
       if (ft < sink_len) {
-        return key ? reinterpret_cast<const uint16_t*>(a.sink_k) + b * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
-                   : reinterpret_cast<const uint16_t*>(a.sink_v) + b * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok;
+        return key ? reinterpret_cast<const uint16_t*>(a.sink_k) + cr * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
+                   : reinterpret_cast<const uint16_t*>(a.sink_v) + cr * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok;
       }
       const int tt = ft - sink_len;
-      return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + b * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
-                 : reinterpret_cast<const uint16_t*>(a.tail_v) + b * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
+      return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + cr * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
+                 : reinterpret_cast<const uint16_t*>(a.tail_v) + cr * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
     };
     // scores: rows = tokens 16 g_ + m / m + 8; k-step s, K indices (2q_, 2q_+1, 2q_+8, 2q_+9)
     // <-> channels 32 q_ + 4 s + (0, 1, 2, 3): the thread reads 64 contiguous bytes per token
@@ -395,7 +396,7 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // physical page of page item pp (>= n16) of sequence bb; out-of-range entries fetch page 0 and are skipped
   auto phys = [&](int bb, int pp, int n16) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - n16)]; };
   auto issue_k = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p, c.n16);
+    int64_t page = phys(c.s, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_k, k_tx);
@@ -404,7 +405,7 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
   };
   auto issue_v = [&](const Cursor& c) {
-    int64_t page = phys(c.b, c.p, c.n16);
+    int64_t page = phys(c.s, c.p, c.n16);
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_v, v_tx);
@@ -425,11 +426,11 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     const int b = pos.b, h = pos.h;
     if (pos.p < pos.n16) {
       int t0, t1;
-      fp16_chunk(fp16_tokens(a, b), pos.n16, pos.p, t0, t1);
+      fp16_chunk(fp16_tokens(a, pos.s), pos.n16, pos.p, t0, t1);
       process_fp16_region(a, b, h, st, wsm, L, qk_scale, lane, t0, t1);
     } else {
       // this page is the producer cursor's current page
-      const int64_t page = phys(b, pos.p, pos.n16);
+      const int64_t page = phys(pos.s, pos.p, pos.n16);
       const bool valid = page >= 0 && page < a.pool_pages;
       if (!mbar_wait(bar_k, k_phase)) { failed = true; break; }
       k_phase ^= 1u;

@@ -89,11 +89,12 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 #pragma unroll
     for (int qh = 0; qh < kMaxGroupSimt; ++qh) o_acc[j][qh] = 0.f;
 
-  const int npages = a.num_pages[b];
+  const int cr = a.seq_map ? a.seq_map[b] : b;   // cache row of batch row b
+  const int npages = a.num_pages[cr];
   const int p_begin = split * plan.pages_per_split;
   const int p_end = min(npages, p_begin + plan.pages_per_split);
-  const int sink_len = a.sink_len ? a.sink_len[b] : a.sink_len_all;
-  const int tail_len = a.tail_len ? a.tail_len[b] : a.tail_len_all;
+  const int sink_len = a.sink_len ? a.sink_len[cr] : a.sink_len_all;
+  const int tail_len = a.tail_len ? a.tail_len[cr] : a.tail_len_all;
   const int fp16_tokens = (split == 0) ? (sink_len + tail_len) : 0;
   const int fp16_chunks = (fp16_tokens + chunk_cap - 1) / chunk_cap;
   const int n_items = fp16_chunks + max(0, p_end - p_begin);
@@ -105,7 +106,7 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     int64_t page = 0;
     int f0 = 0;  // first fp16 token of this chunk (sinks first, then tail)
     if (is_page) {
-      page = a.block_table[b * a.bt_s_seq + p_begin + (item - fp16_chunks)];
+      page = a.block_table[cr * a.bt_s_seq + p_begin + (item - fp16_chunks)];
       if (page < 0 || page >= a.pool_pages) continue;  // out-of-range entries are skipped
       ntok = G;
       // stage the five pool slices
@@ -145,8 +146,8 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         } else {
           const int ft = f0 + t;
           const uint16_t* kp = (ft < sink_len)
-              ? reinterpret_cast<const uint16_t*>(a.sink_k) + b * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
-              : reinterpret_cast<const uint16_t*>(a.tail_k) + b * a.tk_s_seq + h * a.tk_s_head + (ft - sink_len) * a.tk_s_tok;
+              ? reinterpret_cast<const uint16_t*>(a.sink_k) + cr * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
+              : reinterpret_cast<const uint16_t*>(a.tail_k) + cr * a.tk_s_seq + h * a.tk_s_head + (ft - sink_len) * a.tk_s_tok;
           for (int c = 0; c < D; ++c) {
             const float kv = h2f(kp[c]);
 #pragma unroll
@@ -218,8 +219,8 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         for (int t = 0; t < ntok; ++t) {
           const int ft = f0 + t;
           const uint16_t* vp = (ft < sink_len)
-              ? reinterpret_cast<const uint16_t*>(a.sink_v) + b * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok
-              : reinterpret_cast<const uint16_t*>(a.tail_v) + b * a.tv_s_seq + h * a.tv_s_head + (ft - sink_len) * a.tv_s_tok;
+              ? reinterpret_cast<const uint16_t*>(a.sink_v) + cr * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok
+              : reinterpret_cast<const uint16_t*>(a.tail_v) + cr * a.tv_s_seq + h * a.tv_s_head + (ft - sink_len) * a.tv_s_tok;
           const float vv = h2f(vp[c]);
 #pragma unroll
           for (int qh = 0; qh < kMaxGroupSimt; ++qh)

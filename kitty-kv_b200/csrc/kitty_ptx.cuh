@@ -91,7 +91,7 @@ __device__ __forceinline__ uint32_t pack16(uint32_t lo, uint32_t hi) { return lo
 
 // ---- segment walk -----------------------------------------------------------
 //
-// Segment (b, h) has L_b = n16_b + num_pages[b] items: items 0 .. n16_b - 1 are
+// Segment (b, h) has L_b = n16_b + num_pages[row of b] items: items 0 .. n16_b - 1 are
 // chunks of its fp16 region (sinks then tail, at most kMaxFp16Items chunks of
 // about the same length, at least one item even when the region is empty), items
 // n16_b .. are the quantised pages in block-table order.  Splitting the fp16 region
@@ -100,16 +100,20 @@ __device__ __forceinline__ uint32_t pack16(uint32_t lo, uint32_t hi) { return lo
 constexpr int kFp16ChunkTokens = 32;   // a chunk item covers at least this many tokens
 constexpr int kMaxFp16Items = 4;
 
-__device__ __forceinline__ int fp16_tokens(const KittyDecodeArgs& a, int b) {
-  return max(a.sink_len ? a.sink_len[b] : a.sink_len_all, 0) + max(a.tail_len ? a.tail_len[b] : a.tail_len_all, 0);
+// cache row of batch row b (KittyDecodeArgs::seq_map)
+__device__ __forceinline__ int cache_row(const KittyDecodeArgs& a, int b) { return a.seq_map ? a.seq_map[b] : b; }
+
+// fp16 tokens (sinks + tail) of cache row s
+__device__ __forceinline__ int fp16_tokens(const KittyDecodeArgs& a, int s) {
+  return max(a.sink_len ? a.sink_len[s] : a.sink_len_all, 0) + max(a.tail_len ? a.tail_len[s] : a.tail_len_all, 0);
 }
 __device__ __forceinline__ int fp16_items(int tokens) {
   return tokens <= kFp16ChunkTokens ? 1 : min(kMaxFp16Items, (tokens + kFp16ChunkTokens - 1) / kFp16ChunkTokens);
 }
-// items of the segments of sequence b; n16 receives its fp16 items
-__device__ __forceinline__ int seg_items(const KittyDecodeArgs& a, int b, int& n16) {
-  n16 = fp16_items(fp16_tokens(a, b));
-  return n16 + max(a.num_pages[b], 0);
+// items of the segments of cache row s; n16 receives its fp16 items
+__device__ __forceinline__ int seg_items(const KittyDecodeArgs& a, int s, int& n16) {
+  n16 = fp16_items(fp16_tokens(a, s));
+  return n16 + max(a.num_pages[s], 0);
 }
 // tokens [t0, t1) of fp16 chunk c of a region of `tokens` tokens split into n16 chunks
 __device__ __forceinline__ void fp16_chunk(int tokens, int n16, int c, int& t0, int& t1) {
@@ -133,7 +137,7 @@ __device__ inline SegmentScan scan_segments(const KittyDecodeArgs& a, int B, int
   for (int b0 = 0; b0 < B; b0 += 32) {
     const int b = b0 + lane;
     int n16 = 0;
-    const int64_t L = (b < B) ? seg_items(a, b, n16) : 0;
+    const int64_t L = (b < B) ? seg_items(a, cache_row(a, b), n16) : 0;
     const int64_t seq_items = int64_t(H) * L;
     int64_t incl = seq_items;
 #pragma unroll
@@ -163,14 +167,16 @@ __device__ inline SegmentScan scan_segments(const KittyDecodeArgs& a, int B, int
 // the producer cursor that runs ahead over the real pages.
 struct Cursor {
   int64_t f;      // item index
-  int b, h, p;    // sequence, KV head, item in segment
+  int b, h, p;    // sequence (batch row), KV head, item in segment
+  int s;          // cache row of b
   int n16, items; // fp16 items and all items of the current segment
 };
 
 __device__ __forceinline__ Cursor make_cursor(const KittyDecodeArgs& a, int64_t f, int b, int h, int p) {
   Cursor c;
   c.f = f; c.b = b; c.h = h; c.p = p;
-  c.items = seg_items(a, b, c.n16);
+  c.s = cache_row(a, b);
+  c.items = seg_items(a, c.s, c.n16);
   return c;
 }
 
@@ -182,8 +188,9 @@ __device__ __forceinline__ bool cursor_step(Cursor& c, const KittyDecodeArgs& a)
     if (++c.h == a.num_kv_heads) {
       c.h = 0;
       if (++c.b >= a.batch) return false;
+      c.s = cache_row(a, c.b);
     }
-    c.items = seg_items(a, c.b, c.n16);
+    c.items = seg_items(a, c.s, c.n16);
   }
   return true;
 }

@@ -64,6 +64,7 @@ quantize_key_kernel(const KittyKeyQuantArgs a) {
   const uint16_t* src = reinterpret_cast<const uint16_t*>(a.key) + a.key_off[job] + h * a.key_s_head;
   const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
   const int64_t page = a.dst_page[job];
+  if (page < 0) return;   // skipped job (a batched append flushes only full buffers)
 
   stage_block(tile, src, a.key_s_tok, a.key_s_ch, G, D, G);
   const int high_words = (K * G4 + 3) / 4;
@@ -142,6 +143,7 @@ quantize_value_kernel(const KittyValueQuantArgs a) {
   const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) + a.value_off[job] + h * a.val_s_head;
   const int n_valid = a.n_valid ? a.n_valid[job] : G;
   const int64_t page = a.dst_page[job];
+  if (page < 0) return;   // skipped job (a batched append flushes only full buffers)
   stage_block(tile, src, a.val_s_tok, a.val_s_ch, G, D, n_valid);
   __syncthreads();
 
@@ -345,6 +347,7 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
   const uint16_t* src = reinterpret_cast<const uint16_t*>(a.key) + a.key_off[job] + h * a.key_s_head;
   const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
   const int64_t page = a.dst_page[job];
+  if (page < 0) return;   // skipped job (a batched append flushes only full buffers)
 
   Tile8x8 t;
   load_tile(t, src, a.key_s_tok, tg, cg, G);
@@ -482,6 +485,7 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
   const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) + a.value_off[job] + h * a.val_s_head;
   const int n_valid = a.n_valid ? a.n_valid[job] : 128;
   const int64_t page = a.dst_page[job];
+  if (page < 0) return;   // skipped job (a batched append flushes only full buffers)
   Tile8x8 t;
   load_tile(t, src, a.val_s_tok, tg, cg, n_valid);
   uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.val_scale) + page * a.meta_s_page + h * a.meta_s_head;

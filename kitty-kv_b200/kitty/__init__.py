@@ -10,6 +10,7 @@ from .sensitivity import KittySensitivityProfiler
 from .layout import PageCentricKVLayoutManager
 from .pipeline import KittyInferencePipeline
 from .attention import KittyPagedAttention, KittyAttentionFactory
+from .batched import BatchedKVCache
 
 __version__ = "0.1.0+b200"
 __description__ = ("2-bit KV Cache Quantization with per-channel boosted precision and Dense-Sparse "
@@ -22,4 +23,5 @@ __all__ = [
     "KittyInferencePipeline",
     "KittyPagedAttention",
     "KittyAttentionFactory",
+    "BatchedKVCache",
 ]

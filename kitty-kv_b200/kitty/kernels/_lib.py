@@ -16,7 +16,7 @@ from typing import Dict, Optional, Tuple
 
 import torch
 
-ABI_VERSION = 1
+ABI_VERSION = 2
 LIB_NAME = "libkitty_b200.so"
 _LIB_PATH = Path(os.environ.get("KITTY_B200_LIB", Path(__file__).resolve().parent.parent / LIB_NAME))
 
@@ -67,7 +67,18 @@ class DecodeArgs(ctypes.Structure):
                 ("tail_v", c_ptr), ("tv_s_seq", c_i64), ("tv_s_head", c_i64), ("tv_s_tok", c_i64),
                 ("tail_len", c_ptr), ("tail_len_all", c_i32),
                 ("max_pages_per_seq", c_i32), ("num_splits", c_i32),
-                ("workspace", c_ptr), ("workspace_bytes", c_size)]
+                ("workspace", c_ptr), ("workspace_bytes", c_size), ("seq_map", c_ptr)]
+
+
+class CacheState(ctypes.Structure):
+    _fields_ = [("max_seqs", c_i32), ("num_heads", c_i32), ("head_dim", c_i32), ("group", c_i32),
+                ("sink_size", c_i32), ("d_boost", c_i32), ("sentinel", c_i32), ("max_pages_per_seq", c_i32),
+                ("pool_pages", c_i64), ("boost_idx", c_ptr), ("bidx_s_head", c_i64),
+                ("sink_k", c_ptr), ("sink_v", c_ptr), ("tail_k", c_ptr), ("tail_v", c_ptr),
+                ("sink_len", c_ptr), ("tail_len", c_ptr), ("num_pages", c_ptr), ("claim", c_ptr),
+                ("block_table", c_ptr), ("free_pages", c_ptr), ("free_top", c_ptr),
+                ("key_low", c_ptr), ("key_high", c_ptr), ("key_meta", c_ptr), ("val_codes", c_ptr),
+                ("val_meta", c_ptr), ("job_off", c_ptr), ("job_page", c_ptr), ("job_slot", c_ptr)]
 
 
 # Every symbol the header declares, with its ctypes signature.
@@ -84,8 +95,12 @@ SIGNATURES = {
     "kitty_device_error_flags": (ctypes.c_int, [ctypes.POINTER(ctypes.c_uint32), ctypes.c_int]),
     "kitty_paged_decode_noalloc": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
     "kitty_decode_force_variant": (ctypes.c_int, [ctypes.c_int, ctypes.POINTER(ctypes.c_int)]),
+    "kitty_cache_reset": (ctypes.c_int, [ctypes.POINTER(CacheState), c_ptr]),
+    "kitty_cache_append": (ctypes.c_int, [ctypes.POINTER(CacheState), c_i32, c_ptr, c_ptr, c_i64, c_i64,
+                                          c_ptr, c_i64, c_i64, c_ptr]),
+    "kitty_cache_release": (ctypes.c_int, [ctypes.POINTER(CacheState), c_i32, c_ptr, c_ptr]),
 }
-STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs}
+STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs, 4: CacheState}
 
 _lib: Optional[ctypes.CDLL] = None
 _lock = threading.Lock()
@@ -129,11 +144,15 @@ def check(rc: int, what: str) -> None:
 
 
 def device_error_flags(clear: bool = True) -> int:
-    """Sticky device-side error bits (bit 0: a decode wait timed out); synchronises."""
+    """Sticky device-side error bits (bit 0: a decode wait timed out; bits 1-4: cache
+    append / release, ``CACHE_ERRORS``); synchronises."""
     v = ctypes.c_uint32(0)
     check(load().kitty_device_error_flags(ctypes.byref(v), int(clear)), "kitty_device_error_flags")
     return v.value
 
+
+CACHE_ERRORS = {1 << 1: "no free page", 1 << 2: "block table full",
+                1 << 3: "sequence id out of range or repeated in a batch", 1 << 4: "free-page stack overflow"}
 
 DECODE_VARIANTS = {"auto": -1, "simt": 0, "mma": 1, "int8": 2}
 

@@ -69,13 +69,17 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
                             tail_len: Union[int, torch.Tensor, None] = None,
                             out: Optional[torch.Tensor] = None, num_splits: int = 0,
                             sm_scale: Optional[float] = None,
-                            max_pages_per_seq: Optional[int] = None) -> torch.Tensor:
+                            max_pages_per_seq: Optional[int] = None,
+                            seq_map: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Batched decode: q (B, Hq, D) fp16 -> (B, Hq, D) fp16.
 
     block_table (B, maxP) int32 physical pages (row b uses its first
     num_pages[b] entries); pools as in the layout manager; sink_k/v and
     tail_k/v (B, H, S|Q, D) fp16 with per-sequence lengths ``sink_len`` /
     ``tail_len`` (int or (B,) int32 tensor).  Key and value tails share one length.
+    With ``seq_map`` ((B,) int32), row b of q / out reads row seq_map[b] of the
+    block table, page counts, lengths and fp16 regions, which then have one row
+    per cache slot (any number of rows) instead of one per batch row.
     """
     dev = _lib.require_cuda(q, block_table, num_pages, key_baseline, key_boost, key_meta, value_pool,
                             value_meta, boost_idx, sink_k, sink_v, tail_k, tail_v)
@@ -100,12 +104,19 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
         raise RuntimeError("pool shapes are inconsistent")
     if boost_idx.dtype != torch.uint8 or tuple(boost_idx.shape) != (H, D) or boost_idx.stride(1) != 1:
         raise RuntimeError("boost_idx must be (H, D) uint8 with unit channel stride")
-    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] != B:
-        raise RuntimeError("block_table must be (B, maxP) int32")
+    rows = B
+    if seq_map is not None:
+        if seq_map.dtype != torch.int32 or seq_map.numel() != B or seq_map.device != dev:
+            raise RuntimeError("seq_map must be a (B,) int32 tensor on the pools' device")
+        if not seq_map.is_contiguous():
+            seq_map = seq_map.contiguous()
+        rows = block_table.shape[0]
+    if block_table.dtype != torch.int32 or block_table.dim() != 2 or block_table.shape[0] != rows:
+        raise RuntimeError("block_table must be (B, maxP) int32 (one row per cache slot with seq_map)")
     if block_table.stride(1) != 1:
         raise RuntimeError("block_table rows need unit stride")
-    if num_pages.dtype != torch.int32 or num_pages.numel() != B:
-        raise RuntimeError("num_pages must be (B,) int32")
+    if num_pages.dtype != torch.int32 or num_pages.numel() != rows:
+        raise RuntimeError("num_pages must be (B,) int32 (one entry per cache slot with seq_map)")
     if q.dtype != torch.float16:
         q = q.to(torch.float16)
     if q.stride(-1) != 1:
@@ -113,8 +124,8 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
     for t, n in ((sink_k, "sink_k"), (sink_v, "sink_v"), (tail_k, "tail_k"), (tail_v, "tail_v")):
         if t is not None and (t.dtype != torch.float16 or t.dim() != 4 or t.shape[1] != H or t.shape[3] != D):
             raise RuntimeError(f"{n} must be (B, H, T, D) float16")
-    sink_t, sink_all = _as_len(sink_len, "sink_len", B, dev)
-    tail_t, tail_all = _as_len(tail_len, "tail_len", B, dev)
+    sink_t, sink_all = _as_len(sink_len, "sink_len", rows, dev)
+    tail_t, tail_all = _as_len(tail_len, "tail_len", rows, dev)
     if sink_t is None and sink_all > 0 and (sink_k is None or sink_all > min(sink_k.shape[2], sink_v.shape[2])):
         raise RuntimeError("sink_len exceeds the sink tensors")
     if tail_t is None and tail_all > 0 and (tail_k is None or tail_all > min(tail_k.shape[2], tail_v.shape[2])):
@@ -142,6 +153,7 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
     a.tail_v = _lib.ptr(tail_v); a.tv_s_seq, a.tv_s_head, a.tv_s_tok = _strides4(tail_v)
     a.tail_len, a.tail_len_all = _lib.ptr(tail_t), tail_all
     a.max_pages_per_seq, a.num_splits = maxp, int(num_splits)
+    a.seq_map = _lib.ptr(seq_map)
     lib = _lib.load()
     nbytes = _lib.c_size(0)
     _lib.check(lib.kitty_paged_decode_workspace_size(a, nbytes, None), "kitty_paged_decode_workspace_size")

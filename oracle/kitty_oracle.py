@@ -16,6 +16,8 @@ metadata equals the reference's by value:
 * ``dequantize_value_page``<- ``kitty/kernels/quantize_value.py:97-133``
 * ``paged_attention``      <- ``kitty/kernels/attention.py:46-189``
 * ``boost_idx_from_scores``<- ``kitty/sensitivity.py:164-207``
+* ``cache_regions`` / ``sequence_state`` <- ``kitty/pipeline.py:115-181`` (push_token's
+  sink / Q-buffer / flush state machine, values aligned with their keys)
 
 Parity of this restatement is pinned against golden vectors produced by the
 reference itself (``tests/golden/make_golden.py`` imports the reference and
@@ -313,6 +315,42 @@ def paged_attention_batched(q: np.ndarray, block_table: np.ndarray, num_pages: n
                                  val_codes, val_meta, boost_idx, d_boost,
                                  sink_k[b, :, :s], sink_v[b, :, :s], tail_k[b, :, :t],
                                  tail_v[b, :, :t], Hq, H, D)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# per-sequence cache state after a token history (push_token state machine)
+# ---------------------------------------------------------------------------
+
+def cache_regions(n_tokens: int, sink_size: int, group: int) -> Tuple[int, int, int]:
+    """(sink_len, num_pages, tail_len) after ``n_tokens`` pushes: the first S tokens
+    fill the sinks (``kitty/pipeline.py:138-145``), every later token goes to the
+    Key Q-buffer (``:148``) and a buffer reaching G tokens becomes one page and is
+    emptied (``:171-181``)."""
+    s = min(n_tokens, sink_size)
+    rest = n_tokens - s
+    return s, rest // group, rest % group
+
+
+def sequence_state(keys: np.ndarray, values: np.ndarray, sink_size: int, group: int,
+                   boost_idx: np.ndarray, d_boost: int, sentinel: int) -> dict:
+    """Expected cache contents of one sequence whose tokens are keys / values (T, H, D)
+    float16: fp16 sinks and tail, and for each page the quantised key planes (of the
+    (H, D, G) block of its G keys) and value planes (of its G values, the values of
+    the same tokens - the pipeline's aligned-values mode)."""
+    keys = np.asarray(keys, np.float16)
+    values = np.asarray(values, np.float16)
+    s, n, t = cache_regions(keys.shape[0], sink_size, group)
+    out = {"sink_k": keys[:s].transpose(1, 0, 2), "sink_v": values[:s].transpose(1, 0, 2),
+           "tail_k": keys[s + n * group:].transpose(1, 0, 2), "tail_v": values[s + n * group:].transpose(1, 0, 2),
+           "pages": []}
+    for j in range(n):
+        kb = keys[s + j * group: s + (j + 1) * group]          # (G, H, D)
+        vb = values[s + j * group: s + (j + 1) * group]
+        low, high, scale, zero = quantize_key_pages(kb.transpose(1, 2, 0), boost_idx, d_boost, sentinel)
+        codes, vscale, vzero = quantize_value_pages(vb.transpose(1, 0, 2))
+        out["pages"].append({"key_low": low, "key_high": high, "key_scale": scale, "key_zero": zero,
+                             "val_codes": codes, "val_scale": vscale, "val_zero": vzero})
     return out
 
 

@@ -145,3 +145,42 @@ def test_profiler_rule_matches_reference(golden_manifest):
     keys = [GC.synthetic.make_kv(rng, 4, 256, 128)[0] for _ in range(2)]
     mine = np.stack([O.boost_idx_from_scores(GC.synthetic.channel_scores([k]), 16, 17) for k in keys])
     assert sha(mine) == golden_manifest["profiler"]["boost_idx_sha"]
+
+
+@pytest.mark.parametrize("name", ["tiny", "d128"])
+def test_sequence_state_matches_reference_pipeline(golden_npz, golden_manifest, name):
+    """The cache state machine of the oracle (sinks, key pages, key tail after T pushes)
+    against the reference pipeline driven over the same tokens: counters, the page
+    count, the key pool bytes and the fp16 sink / Key Q-buffer contents.  (Value pages
+    are not compared: the reference quantises its value window's evictions, the
+    batched cache the values of the page's own tokens.)"""
+    from kitty import synthetic
+    e = golden_manifest["pipeline"][name]
+    cfg = e["config"]
+    H, D, G, S = cfg["num_kv_heads"], cfg["head_dim"], cfg["q_buffer_size"], cfg["sink_size"]
+    K = round(cfg["boost_rate"] * D)
+    sent = min(K + 1, 255)
+    rng = np.random.default_rng(e["seed"])
+    k, v = synthetic.make_kv(rng, H, e["steps"], D)
+    bidx = synthetic.boost_idx_from_scores(synthetic.channel_scores([k]), K, sent)
+    st = O.sequence_state(k.transpose(1, 0, 2), v.transpose(1, 0, 2), S, G, bidx, K, sent)
+    s, n, t = O.cache_regions(e["steps"], S, G)
+    assert (s, t) == (e["state"]["sink_fill"], e["state"]["key_qbuf_len"])
+    assert n == len(e["page_list"]) == len(st["pages"])
+    P = ((cfg["max_seq_len"] - S) // G + 2)
+    low = np.zeros((P, H, D, G // 4), np.uint8)
+    high = np.zeros((P, H, K, G // 4), np.uint8)
+    meta = np.zeros((P, H, 2, D), np.float16)
+    for j, page in enumerate(e["page_list"]):
+        pg = st["pages"][j]
+        low[page], high[page] = pg["key_low"], pg["key_high"]
+        meta[page, :, 0], meta[page, :, 1] = pg["key_scale"], pg["key_zero"]
+    assert sha(low) == e["pools_sha"]["key_low"]
+    assert sha(high) == e["pools_sha"]["key_high"]
+    assert sha(meta_by_value(meta)) == e["pools_sha"]["key_meta_value"]
+    sink = np.zeros((1, H, S, D), np.float16)
+    sink[0, :, :s] = st["sink_k"]
+    assert sha(sink) == e["buffers_sha"]["sink_k"]
+    qbuf = np.zeros((1, H, G, D), np.float16)
+    qbuf[0, :, :t] = st["tail_k"]
+    assert sha(qbuf) == e["buffers_sha"]["key_qbuf"]
