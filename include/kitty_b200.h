@@ -47,8 +47,8 @@ const char* kitty_last_error(void);
 
 /* sizeof() of the argument structs below, so a foreign-function binding can
  * check its mirror of them: kind 0 = KittyKeyQuantArgs, 1 = KittyValueQuantArgs,
- * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs, 4 = KittyCacheState; 0 for an
- * unknown kind. */
+ * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs, 4 = KittyCacheState,
+ * 5 = KittyPrefillArgs; 0 for an unknown kind. */
 size_t kitty_args_size(int kind);
 
 /* ---------------------------------------------------------------------------
@@ -297,6 +297,42 @@ int kitty_cache_append(const KittyCacheState* state, int32_t n, const int32_t* s
                        const void* key, int64_t k_s_tok, int64_t k_s_head,
                        const void* value, int64_t v_s_tok, int64_t v_s_head, void* stream);
 
+/* Bulk append of many tokens per sequence (a prefill, or a chunk of one).
+ *
+ * Replaces KittyPagedAttention._prefill's per-token push loop
+ * (kitty/attention.py:153-191, kitty/pipeline.py:115-181).  Sequence
+ * seq_ids[i] receives lengths[i] tokens: source rows row_start[i] ..
+ * row_start[i] + lengths[i] - 1, row r / head h at key + r*s_tok + h*s_head
+ * (value likewise, same strides; 16-byte aligned rows).  The result equals
+ * appending those tokens one by one with kitty_cache_append: sinks first, then
+ * the G-token buffer; a buffer that fills is quantised into a new page, and
+ * every further full group of G tokens is quantised straight from the source
+ * rows into its own page (bit-exact with the page quantisers).  Seven launches,
+ * no host synchronisation.
+ *
+ * max_pages bounds the pages quantised straight from the source in this call
+ * (sum over i of lengths[i] / G is always enough); page_off / page_dst are
+ * scratch of max_pages entries and seq_plan of 6 n entries (device memory).
+ * Sequences are served in order; a sequence whose pages do not fit (free stack,
+ * its block table, or max_pages) is left unchanged and sets error bit 1, 2 or
+ * 5 — once one has failed for want of pages, the later ones that need pages
+ * fail too.  Ids out of range or repeated set bit 3. */
+typedef struct KittyPrefillArgs {
+  int32_t n;
+  const int32_t* seq_ids;     /* [n] */
+  const int32_t* lengths;     /* [n] tokens per sequence (>= 0) */
+  const int64_t* row_start;   /* [n] first source row of each sequence */
+  const void* key;            /* fp16 */
+  const void* value;          /* fp16 */
+  int64_t s_tok, s_head;      /* element strides of a row / a head in key and value */
+  int32_t max_pages;
+  int64_t* page_off;          /* [max_pages] scratch */
+  int32_t* page_dst;          /* [max_pages] scratch */
+  int32_t* seq_plan;          /* [6 n] scratch */
+} KittyPrefillArgs;
+
+int kitty_cache_prefill(const KittyCacheState* state, const KittyPrefillArgs* args, void* stream);
+
 /* Empty the n sequences seq_ids[i] (device memory) and push their pages back on
  * the free stack (in block-table order, sequence after sequence).  Releasing an
  * empty sequence is a no-op; ids out of range set error bit 3; a stack that
@@ -305,7 +341,7 @@ int kitty_cache_release(const KittyCacheState* state, int32_t n, const int32_t* 
 
 /* Sticky error bits set by device code on the current device (bit 0: a decode
  * kernel gave up waiting for a bulk copy after its bounded wait and returned
- * without a valid result; bits 1-4: kitty_cache_append / kitty_cache_release,
+ * without a valid result; bits 1-5: kitty_cache_append / _prefill / _release,
  * above).  Synchronises with the device; clear != 0 resets the bits after
  * reading them. */
 int kitty_device_error_flags(uint32_t* flags, int clear);

@@ -128,6 +128,7 @@ size_t kitty_args_size(int kind) {
     case 2: return sizeof(KittyKeyDequantArgs);
     case 3: return sizeof(KittyDecodeArgs);
     case 4: return sizeof(KittyCacheState);
+    case 5: return sizeof(KittyPrefillArgs);
     default: return 0;
   }
 }

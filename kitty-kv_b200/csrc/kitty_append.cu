@@ -1,5 +1,5 @@
-// Device-resident cache state: batched append with in-step page flushes, release
-// and reset (kitty_cache_* in the C ABI).
+// Device-resident cache state: batched append with in-step page flushes, bulk
+// append (prefill), release and reset (kitty_cache_* in the C ABI).
 //
 // A decode step of n sequences runs four launches and no host synchronisation:
 //   1. append_plan_kernel (one CTA): per token, the sequence's next slot (a sink
@@ -9,6 +9,8 @@
 //   2. append_copy_kernel: the fp16 key / value rows into their slots (16-byte
 //      vectors), and the duplicate-detection claims cleared;
 //   3. + 4. the page quantisers over the recorded jobs (jobs without a page skip).
+// A prefill (many tokens per sequence) plans every sequence at once in the same
+// way and quantises all full G-token groups straight from the source rows.
 // The state machine per sequence is the reference pipeline's push_token
 // (kitty/pipeline.py:115-181: sinks first, then the Key Q-buffer, a flush when it
 // holds G tokens) with the values of the same tokens in a parallel buffer, and
@@ -33,6 +35,7 @@ constexpr uint32_t kErrNoPage = 1u << 1;      // free stack empty
 constexpr uint32_t kErrTableFull = 1u << 2;   // block table row full
 constexpr uint32_t kErrBadSeq = 1u << 3;      // id out of range or repeated in one batch
 constexpr uint32_t kErrOverflow = 1u << 4;    // release would overflow the stack
+constexpr uint32_t kErrBudget = 1u << 5;      // prefill: more source pages than max_pages
 
 constexpr int kPlanThreads = 1024;
 constexpr int32_t kTailSlot = 1 << 30;        // job_slot: kTailSlot | pos = buffer slot, pos = sink slot
@@ -165,6 +168,131 @@ __global__ void append_copy_kernel(KittyCacheState st, int n, const int32_t* __r
   }
 }
 
+// ---- bulk append (prefill) ---------------------------------------------------
+//
+// Per sequence (one thread): a = tokens to the sinks, pre = tokens completing a
+// partly filled buffer (flush = it becomes full), m = full G-token groups quantised
+// straight from the source rows, rem = tokens left in the (then empty) buffer.
+// Pages: the flushed buffer's first, then the m source pages, all from the free
+// stack in sequence order; job slots of the source pages by prefix sum.
+constexpr int kPlanInts = 6;   // seq_plan: sink_len, a, tail_len, pre, rem, m
+
+__global__ void __launch_bounds__(kPlanThreads) prefill_plan_kernel(KittyCacheState st, KittyPrefillArgs p) {
+  __shared__ int s_warp[33];
+  __shared__ int s_top, s_jobs;
+  if (threadIdx.x == 0) { s_top = *st.free_top; s_jobs = 0; }
+  for (int j = threadIdx.x; j < p.max_pages; j += kPlanThreads) p.page_dst[j] = -1;
+  __syncthreads();
+  const int S = st.sink_size, G = st.group;
+  const int64_t buf_elems = int64_t(st.num_heads) * G * st.head_dim;
+  uint32_t err = 0;
+  for (int base = 0; base < p.n; base += kPlanThreads) {
+    const int i = base + threadIdx.x;
+    int s = -1, sl = 0, tl = 0, np = 0, a = 0, pre = 0, flush = 0, m = 0, rem = 0, need = 0;
+    if (i < p.n) {
+      s = p.seq_ids[i];
+      const int T = p.lengths[i];
+      if (s < 0 || s >= st.max_seqs || T < 0) {
+        err |= kErrBadSeq; s = -1;
+      } else if (atomicExch(st.claim + s, 1) != 0) {
+        err |= kErrBadSeq; s = -1;
+      }
+      if (s >= 0) {
+        sl = st.sink_len[s]; tl = st.tail_len[s]; np = st.num_pages[s];
+        a = min(max(S - sl, 0), T);
+        int r = T - a;
+        if (r > 0 && tl > 0) { pre = min(G - tl, r); r -= pre; flush = (tl + pre == G) ? 1 : 0; }
+        if (r > 0) { m = r / G; rem = r - m * G; }
+        need = flush + m;
+        if (np + need > st.max_pages_per_seq) { err |= kErrTableFull; s = -1; need = 0; m = 0; }
+      }
+    }
+    int total = 0;
+    const int rank_need = block_exclusive_scan(need, s_warp, &total);
+    const int rank_m = block_exclusive_scan(m, s_warp, &total);
+    const int top = s_top, jobs = s_jobs;
+    bool ok = s >= 0;
+    if (ok && need > 0 && top - rank_need - need < 0) { ok = false; err |= kErrNoPage; }
+    if (ok && m > 0 && int64_t(jobs) + rank_m + m > p.max_pages) { ok = false; err |= kErrBudget; }
+    int total_need = 0, total_m = 0;
+    const int r2 = block_exclusive_scan(ok ? need : 0, s_warp, &total_need);
+    const int rm2 = block_exclusive_scan(ok ? m : 0, s_warp, &total_m);
+    if (i < p.n) {
+      int* plan = p.seq_plan + int64_t(kPlanInts) * i;
+      st.job_page[i] = -1;
+      st.job_off[i] = 0;
+      if (ok) {
+        int32_t* row = st.block_table + int64_t(s) * st.max_pages_per_seq + np;
+        int k = 0;
+        if (flush) {
+          const int page = st.free_pages[top - 1 - r2];
+          row[0] = page;
+          st.job_page[i] = page;
+          st.job_off[i] = int64_t(s) * buf_elems;
+          k = 1;
+        }
+        const int64_t first = p.row_start[i] + a + pre;
+        for (int j = 0; j < m; ++j) {
+          const int page = st.free_pages[top - 1 - r2 - k - j];
+          row[k + j] = page;
+          p.page_dst[jobs + rm2 + j] = page;
+          p.page_off[jobs + rm2 + j] = (first + int64_t(j) * G) * p.s_tok;
+        }
+        st.sink_len[s] = sl + a;
+        st.num_pages[s] = np + need;
+        st.tail_len[s] = flush ? rem : tl + pre + rem;
+        plan[0] = sl; plan[1] = a; plan[2] = tl; plan[3] = pre; plan[4] = rem; plan[5] = m;
+      } else {
+        plan[0] = plan[1] = plan[2] = plan[3] = plan[4] = plan[5] = 0;
+      }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) { s_top = top - total_need; s_jobs = jobs + total_m; }
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) *st.free_top = s_top;
+  if (err) atomicOr(&g_cache_error, err);
+}
+
+// One CTA per sequence.  Phase 0: the sink tokens and the tokens completing the
+// buffer; phase 1 (after the buffer was quantised): the remaining tokens into the
+// emptied buffer, and the claims cleared.
+__global__ void prefill_copy_kernel(KittyCacheState st, KittyPrefillArgs p, int phase) {
+  const int i = blockIdx.x;
+  const int s = p.seq_ids[i];
+  if (s < 0 || s >= st.max_seqs) return;
+  const int* plan = p.seq_plan + int64_t(kPlanInts) * i;
+  const int sl = plan[0], a = plan[1], tl = plan[2], pre = plan[3], rem = plan[4], m = plan[5];
+  const int H = st.num_heads, D = st.head_dim, S = st.sink_size, G = st.group;
+  const int vecs = D / 8;
+  const int64_t r0 = p.row_start[i];
+  const int count = phase == 0 ? a + pre : rem;
+  const int64_t per_tok = int64_t(H) * 2 * vecs;
+  for (int64_t u = threadIdx.x; u < int64_t(count) * per_tok; u += blockDim.x) {
+    const int t = int(u / per_tok);
+    int r = int(u - int64_t(t) * per_tok);
+    const int which = r / (H * vecs);
+    r -= which * H * vecs;
+    const int h = r / vecs, v = r - h * vecs;
+    int64_t src_row;
+    uint16_t* dst;
+    if (phase == 0 && t < a) {
+      src_row = r0 + t;
+      uint16_t* b = static_cast<uint16_t*>(which == 0 ? st.sink_k : st.sink_v);
+      dst = b + ((int64_t(s) * H + h) * S + sl + t) * D;
+    } else {
+      const int pos = phase == 0 ? tl + (t - a) : t;
+      src_row = phase == 0 ? r0 + t : r0 + a + pre + int64_t(m) * G + t;
+      uint16_t* b = static_cast<uint16_t*>(which == 0 ? st.tail_k : st.tail_v);
+      dst = b + ((int64_t(s) * H + h) * G + pos) * D;
+    }
+    const uint16_t* src = static_cast<const uint16_t*>(which == 0 ? p.key : p.value) + src_row * p.s_tok +
+                          h * p.s_head;
+    reinterpret_cast<uint4*>(dst)[v] = __ldg(reinterpret_cast<const uint4*>(src) + v);
+  }
+  if (phase == 1 && threadIdx.x == 0) st.claim[s] = 0;
+}
+
 // One CTA: pages of the released sequences pushed in token order (prefix sum of
 // the page counts), counters zeroed.  num_pages is taken with atomicExch, so an id
 // repeated in the batch pushes its pages once.  A chunk whose pages would overflow
@@ -262,6 +390,39 @@ int read_cache_error(uint32_t* flags, int clear) {
   return KITTY_OK;
 }
 
+// Key and value quantisation of n_jobs page jobs: source element (t, h, c) of job j
+// at base + off[j] + h*s_head + t*s_tok + c, destination page dst[j] (< 0 skips).
+int quantize_pages(const KittyCacheState& st, int n_jobs, const void* key, const void* value, const int64_t* off,
+                   const int32_t* dst, int64_t s_head, int64_t s_tok, void* stream) {
+  if (n_jobs == 0) return KITTY_OK;
+  const int H = st.num_heads, D = st.head_dim, G = st.group, K = st.d_boost;
+  KittyKeyQuantArgs ka{};
+  ka.key = key; ka.key_off = off;
+  ka.key_s_head = s_head; ka.key_s_tok = s_tok; ka.key_s_ch = 1;
+  ka.boost_idx = st.boost_idx; ka.bidx_s_head = st.bidx_s_head;
+  ka.dst_page = dst;
+  ka.key_low = st.key_low; ka.key_high = st.key_high;
+  ka.key_scale = st.key_meta;
+  ka.key_zero = static_cast<uint16_t*>(st.key_meta) + D;
+  ka.low_s_page = int64_t(H) * D * (G / 4); ka.low_s_head = int64_t(D) * (G / 4);
+  ka.high_s_page = int64_t(H) * K * (G / 4); ka.high_s_head = int64_t(K) * (G / 4);
+  ka.meta_s_page = int64_t(H) * 2 * D; ka.meta_s_head = 2 * D;
+  ka.n_jobs = n_jobs; ka.num_heads = H; ka.head_dim = D; ka.group = G; ka.d_boost = K; ka.sentinel = st.sentinel;
+  int rc = quantize_key_pages_impl(&ka, stream);
+  if (rc != KITTY_OK) return rc;
+  KittyValueQuantArgs va{};
+  va.value = value; va.value_off = off;
+  va.val_s_head = s_head; va.val_s_tok = s_tok; va.val_s_ch = 1;
+  va.n_valid = nullptr; va.dst_page = dst;
+  va.val_codes = st.val_codes;
+  va.val_scale = st.val_meta;
+  va.val_zero = static_cast<uint16_t*>(st.val_meta) + 1;
+  va.codes_s_page = int64_t(H) * G * (D / 4); va.codes_s_head = int64_t(G) * (D / 4);
+  va.meta_s_page = int64_t(H) * G * 2; va.meta_s_head = int64_t(G) * 2; va.meta_s_tok = 2;
+  va.n_jobs = n_jobs; va.num_heads = H; va.head_dim = D; va.group = G;
+  return quantize_value_pages_impl(&va, stream);
+}
+
 int cache_reset_impl(const KittyCacheState* st, void* stream) {
   int rc = validate_state(st, "cache_reset");
   if (rc != KITTY_OK) return rc;
@@ -294,33 +455,40 @@ int cache_append_impl(const KittyCacheState* st, int32_t n, const int32_t* seq_i
   rc = check_launch("cache_append (copy)");
   if (rc != KITTY_OK) return rc;
 
-  const int H = st->num_heads, D = st->head_dim, G = st->group, K = st->d_boost;
-  KittyKeyQuantArgs ka{};
-  ka.key = st->tail_k; ka.key_off = st->job_off;
-  ka.key_s_head = int64_t(G) * D; ka.key_s_tok = D; ka.key_s_ch = 1;
-  ka.boost_idx = st->boost_idx; ka.bidx_s_head = st->bidx_s_head;
-  ka.dst_page = st->job_page;
-  ka.key_low = st->key_low; ka.key_high = st->key_high;
-  ka.key_scale = st->key_meta;
-  ka.key_zero = static_cast<uint16_t*>(st->key_meta) + D;
-  ka.low_s_page = int64_t(H) * D * (G / 4); ka.low_s_head = int64_t(D) * (G / 4);
-  ka.high_s_page = int64_t(H) * K * (G / 4); ka.high_s_head = int64_t(K) * (G / 4);
-  ka.meta_s_page = int64_t(H) * 2 * D; ka.meta_s_head = 2 * D;
-  ka.n_jobs = n; ka.num_heads = H; ka.head_dim = D; ka.group = G; ka.d_boost = K; ka.sentinel = st->sentinel;
-  rc = quantize_key_pages_impl(&ka, stream);
-  if (rc != KITTY_OK) return rc;
+  return quantize_pages(*st, n, st->tail_k, st->tail_v, st->job_off, st->job_page,
+                        int64_t(st->group) * st->head_dim, st->head_dim, stream);
+}
 
-  KittyValueQuantArgs va{};
-  va.value = st->tail_v; va.value_off = st->job_off;
-  va.val_s_head = int64_t(G) * D; va.val_s_tok = D; va.val_s_ch = 1;
-  va.n_valid = nullptr; va.dst_page = st->job_page;
-  va.val_codes = st->val_codes;
-  va.val_scale = st->val_meta;
-  va.val_zero = static_cast<uint16_t*>(st->val_meta) + 1;
-  va.codes_s_page = int64_t(H) * G * (D / 4); va.codes_s_head = int64_t(G) * (D / 4);
-  va.meta_s_page = int64_t(H) * G * 2; va.meta_s_head = int64_t(G) * 2; va.meta_s_tok = 2;
-  va.n_jobs = n; va.num_heads = H; va.head_dim = D; va.group = G;
-  return quantize_value_pages_impl(&va, stream);
+int cache_prefill_impl(const KittyCacheState* st, const KittyPrefillArgs* p, void* stream) {
+  int rc = validate_state(st, "cache_prefill");
+  if (rc != KITTY_OK) return rc;
+  if (!p) return fail(KITTY_ERR_INVALID_ARGUMENT, "cache_prefill: args is NULL");
+  if (p->n < 0 || p->n > st->max_seqs)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "cache_prefill: n must be in [0, max_seqs]");
+  if (p->max_pages < 0) return fail(KITTY_ERR_INVALID_ARGUMENT, "cache_prefill: negative max_pages");
+  if (p->n == 0) return KITTY_OK;
+  if (!p->seq_ids || !p->lengths || !p->row_start || !p->key || !p->value || !p->seq_plan ||
+      (p->max_pages > 0 && (!p->page_off || !p->page_dst)))
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "cache_prefill: NULL pointer");
+  if (!aligned(p->key, 16) || !aligned(p->value, 16) || p->s_tok % 8 || p->s_head % 8 || p->s_tok < 0 ||
+      p->s_head < 0)
+    return fail(KITTY_ERR_INVALID_ARGUMENT,
+                "cache_prefill: key/value rows must be 16-byte aligned (strides multiples of 8 elements)");
+  cudaStream_t s = as_stream(stream);
+  prefill_plan_kernel<<<1, kPlanThreads, 0, s>>>(*st, *p);
+  rc = check_launch("cache_prefill (plan)");
+  if (rc != KITTY_OK) return rc;
+  prefill_copy_kernel<<<p->n, 256, 0, s>>>(*st, *p, 0);
+  rc = check_launch("cache_prefill (copy)");
+  if (rc != KITTY_OK) return rc;
+  // buffers that filled, then the full groups straight from the source rows
+  rc = quantize_pages(*st, p->n, st->tail_k, st->tail_v, st->job_off, st->job_page,
+                      int64_t(st->group) * st->head_dim, st->head_dim, stream);
+  if (rc != KITTY_OK) return rc;
+  rc = quantize_pages(*st, p->max_pages, p->key, p->value, p->page_off, p->page_dst, p->s_head, p->s_tok, stream);
+  if (rc != KITTY_OK) return rc;
+  prefill_copy_kernel<<<p->n, 256, 0, s>>>(*st, *p, 1);
+  return check_launch("cache_prefill (copy)");
 }
 
 int cache_release_impl(const KittyCacheState* st, int32_t n, const int32_t* seq_ids, void* stream) {
@@ -347,6 +515,11 @@ int kitty_cache_append(const KittyCacheState* state, int32_t n, const int32_t* s
                        void* stream) {
   kitty::clear_error();
   return kitty::cache_append_impl(state, n, seq_ids, key, k_s_tok, k_s_head, value, v_s_tok, v_s_head, stream);
+}
+
+int kitty_cache_prefill(const KittyCacheState* state, const KittyPrefillArgs* args, void* stream) {
+  kitty::clear_error();
+  return kitty::cache_prefill_impl(state, args, stream);
 }
 
 int kitty_cache_release(const KittyCacheState* state, int32_t n, const int32_t* seq_ids, void* stream) {

@@ -154,6 +154,43 @@ class BatchedKVCache:
                                           key.stride(0), key.stride(1), value.data_ptr(), value.stride(0),
                                           value.stride(1), self._stream()), "kitty_cache_append")
 
+    def prefill(self, layer_id: int, seq_ids, key: torch.Tensor, value: torch.Tensor, lengths) -> None:
+        """Append lengths[i] tokens to slot seq_ids[i] of ``layer_id`` in one call: the
+        tokens of the i-th sequence are the next lengths[i] rows of key / value
+        ((sum(lengths), H, D) float16, sequences one after another).  Same result as
+        appending them one at a time; full groups of G tokens are quantised straight
+        from ``key`` / ``value``.  ``lengths``: host integers (they size the launch)."""
+        lens = [int(x) for x in (lengths.tolist() if isinstance(lengths, torch.Tensor) else lengths)]
+        ids = self._ids(seq_ids)
+        n = ids.numel()
+        if len(lens) != n or min(lens, default=0) < 0:
+            raise RuntimeError("lengths must hold one non-negative count per sequence id")
+        H, D, G = self.config.num_kv_heads, self.config.head_dim, self.config.q_buffer_size
+        N = sum(lens)
+        for t, name in ((key, "key"), (value, "value")):
+            if t.dtype != torch.float16 or t.device != self.device or tuple(t.shape) != (N, H, D):
+                raise RuntimeError(f"{name} must be ({N}, {H}, {D}) float16 on {self.device}")
+        if key.stride(2) != 1 or key.stride() != value.stride():
+            key, value = key.contiguous(), value.contiguous()
+        starts = [0] * n
+        for i in range(1, n):
+            starts[i] = starts[i - 1] + lens[i - 1]
+        dev = self.device
+        host = torch.tensor(lens + [0] * (2 * n), dtype=torch.int64).pin_memory()
+        host[n:2 * n] = torch.tensor(starts, dtype=torch.int64)
+        meta = host.to(dev, non_blocking=True)
+        lens_d = meta[:n].to(torch.int32)
+        max_pages = sum(x // G for x in lens)
+        page_off = torch.empty(max(max_pages, 1), dtype=torch.int64, device=dev)
+        page_dst = torch.empty(max(max_pages, 1), dtype=torch.int32, device=dev)
+        plan = torch.empty(6 * n, dtype=torch.int32, device=dev)
+        a = _lib.PrefillArgs()
+        a.n, a.seq_ids, a.lengths, a.row_start = n, ids.data_ptr(), lens_d.data_ptr(), meta[n:2 * n].data_ptr()
+        a.key, a.value, a.s_tok, a.s_head = key.data_ptr(), value.data_ptr(), key.stride(0), key.stride(1)
+        a.max_pages, a.page_off, a.page_dst, a.seq_plan = max_pages, page_off.data_ptr(), page_dst.data_ptr(), \
+            plan.data_ptr()
+        _lib.check(_lib.load().kitty_cache_prefill(self._states[layer_id], a, self._stream()), "kitty_cache_prefill")
+
     def release(self, seq_ids) -> None:
         """Empty the given slots in every layer and return their pages to the stack."""
         ids = self._ids(seq_ids)

@@ -81,6 +81,12 @@ class CacheState(ctypes.Structure):
                 ("val_meta", c_ptr), ("job_off", c_ptr), ("job_page", c_ptr), ("job_slot", c_ptr)]
 
 
+class PrefillArgs(ctypes.Structure):
+    _fields_ = [("n", c_i32), ("seq_ids", c_ptr), ("lengths", c_ptr), ("row_start", c_ptr),
+                ("key", c_ptr), ("value", c_ptr), ("s_tok", c_i64), ("s_head", c_i64), ("max_pages", c_i32),
+                ("page_off", c_ptr), ("page_dst", c_ptr), ("seq_plan", c_ptr)]
+
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "kitty_abi_version": (ctypes.c_int, []),
@@ -98,9 +104,10 @@ SIGNATURES = {
     "kitty_cache_reset": (ctypes.c_int, [ctypes.POINTER(CacheState), c_ptr]),
     "kitty_cache_append": (ctypes.c_int, [ctypes.POINTER(CacheState), c_i32, c_ptr, c_ptr, c_i64, c_i64,
                                           c_ptr, c_i64, c_i64, c_ptr]),
+    "kitty_cache_prefill": (ctypes.c_int, [ctypes.POINTER(CacheState), ctypes.POINTER(PrefillArgs), c_ptr]),
     "kitty_cache_release": (ctypes.c_int, [ctypes.POINTER(CacheState), c_i32, c_ptr, c_ptr]),
 }
-STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs, 4: CacheState}
+STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs, 4: CacheState, 5: PrefillArgs}
 
 _lib: Optional[ctypes.CDLL] = None
 _lock = threading.Lock()
@@ -144,15 +151,16 @@ def check(rc: int, what: str) -> None:
 
 
 def device_error_flags(clear: bool = True) -> int:
-    """Sticky device-side error bits (bit 0: a decode wait timed out; bits 1-4: cache
-    append / release, ``CACHE_ERRORS``); synchronises."""
+    """Sticky device-side error bits (bit 0: a decode wait timed out; bits 1-5: cache
+    append / prefill / release, ``CACHE_ERRORS``); synchronises."""
     v = ctypes.c_uint32(0)
     check(load().kitty_device_error_flags(ctypes.byref(v), int(clear)), "kitty_device_error_flags")
     return v.value
 
 
 CACHE_ERRORS = {1 << 1: "no free page", 1 << 2: "block table full",
-                1 << 3: "sequence id out of range or repeated in a batch", 1 << 4: "free-page stack overflow"}
+                1 << 3: "sequence id out of range or repeated in a batch", 1 << 4: "free-page stack overflow",
+                1 << 5: "prefill page budget (max_pages) too small"}
 
 DECODE_VARIANTS = {"auto": -1, "simt": 0, "mma": 1, "int8": 2}
 

@@ -271,3 +271,75 @@ def test_decode_step_in_cuda_graph():
         exp = oracle_decode(cache, cfg, l, s, q[t, i])
         np.testing.assert_allclose(o[i].float().cpu().numpy(), exp.astype(np.float32), atol=ATOL, rtol=RTOL)
     del g
+
+
+@pytest.mark.parametrize("name", ["d128", "g16", "tiny"])
+def test_prefill_matches_token_by_token_oracle(name):
+    """Bulk append (prefill) on top of existing states - empty slots, slots inside
+    their sinks, slots with a partly filled buffer - in two chunks, then a decode
+    step: every slot must equal the oracle state of its whole token history."""
+    max_seqs = 6
+    cfg, cache, bidx, rng = make_cache(name, max_seqs, seed=21)
+    L, H, D, S, G = cfg.num_layers, cfg.num_kv_heads, cfg.head_dim, cfg.sink_size, cfg.q_buffer_size
+    pre_len = [0, max(S // 2, 1), S + 3, S + G - 1, S + G + 5, 0]           # tokens appended first
+    chunk1 = [2 * G + 3, G, G + 1, 1, 3 * G, 0]                             # first prefill chunk
+    chunk2 = [G - 1, 0, 2 * G, G + 2, 5, S + G + 7]                          # second chunk
+    total = [a + b + c + 1 for a, b, c in zip(pre_len, chunk1, chunk2)]
+    hist = {(l, s): [x.transpose(1, 0, 2) for x in synthetic.make_kv(rng, H, total[s], D)]
+            for l in range(L) for s in range(max_seqs)}
+    for l in range(L):
+        for t in range(max(pre_len)):
+            ids = [s for s in range(max_seqs) if t < pre_len[s]]
+            k = np.stack([hist[(l, s)][0][t] for s in ids]); v = np.stack([hist[(l, s)][1][t] for s in ids])
+            cache.append(l, ids, torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV))
+    pos = list(pre_len)
+    for chunk in (chunk1, chunk2):
+        order = [int(s) for s in rng.permutation(max_seqs)]
+        for l in range(L):
+            k = np.concatenate([hist[(l, s)][0][pos[s]:pos[s] + chunk[s]] for s in order])
+            v = np.concatenate([hist[(l, s)][1][pos[s]:pos[s] + chunk[s]] for s in order])
+            cache.prefill(l, order, torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV),
+                          [chunk[s] for s in order])
+        for s in range(max_seqs):
+            pos[s] += chunk[s]
+    # one more decode-step append, then compare everything
+    for l in range(L):
+        k = np.stack([hist[(l, s)][0][pos[s]] for s in range(max_seqs)])
+        v = np.stack([hist[(l, s)][1][pos[s]] for s in range(max_seqs)])
+        cache.append(l, list(range(max_seqs)), torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV))
+    torch.cuda.synchronize()
+    cache.check_errors()
+    for (l, s), (k, v) in hist.items():
+        check_sequence(cache, cfg, bidx, l, s, k, v)
+    Hq = 2 * H
+    ids = np.array([5, 0, 3], dtype=np.int32)
+    q = synthetic.make_q(rng, (3, Hq, D))
+    out = cache.decode(L - 1, torch.from_numpy(q).to(DEV), torch.from_numpy(ids).to(DEV))
+    torch.cuda.synchronize()
+    for i, s in enumerate(ids):
+        exp = oracle_decode(cache, cfg, L - 1, int(s), q[i])
+        np.testing.assert_allclose(out[i].float().cpu().numpy(), exp.astype(np.float32), atol=ATOL, rtol=RTOL)
+
+
+def test_prefill_out_of_pages_serves_sequences_in_order():
+    cfg, cache, bidx, rng = make_cache("tiny", 4, seed=23, num_pages=5)
+    H, D, S, G = cfg.num_kv_heads, cfg.head_dim, cfg.sink_size, cfg.q_buffer_size
+    lens = [S + 2 * G, S + 2 * G + 1, S + 3 * G, S + G - 2]     # pages needed: 2, 2, 3, 0
+    kv = [[x.transpose(1, 0, 2) for x in synthetic.make_kv(rng, H, n, D)] for n in lens]
+    k = np.concatenate([x[0] for x in kv]); v = np.concatenate([x[1] for x in kv])
+    cache.prefill(0, [0, 1, 2, 3], torch.from_numpy(k).to(DEV), torch.from_numpy(v).to(DEV), lens)
+    torch.cuda.synchronize()
+    assert _lib.device_error_flags(clear=True) == 1 << 1
+    # sequences 0 and 1 took 4 of the 5 pages; sequence 2 needed 3 and is unchanged;
+    # sequence 3 needs no page and is served
+    for s in (0, 1, 3):
+        check_sequence(cache, cfg, bidx, 0, s, kv[s][0], kv[s][1])
+    assert [int(x) for x in cache.lengths(0)["sink_len"]] == [S, S, 0, S]
+    assert cache.free_page_count() == 1
+    # with pages released, sequence 2's prefill goes through
+    cache.release([0])
+    cache.prefill(0, [2], torch.from_numpy(kv[2][0]).to(DEV), torch.from_numpy(kv[2][1]).to(DEV), [lens[2]])
+    torch.cuda.synchronize()
+    cache.check_errors()
+    check_sequence(cache, cfg, bidx, 0, 2, kv[2][0], kv[2][1])
+    assert cache.free_page_count() == 0
