@@ -30,18 +30,20 @@
 // both digits of the same (token, query head) and combines them with one
 // integer multiply-add: no exchange between lanes, and after the key
 // contraction lane (g_, q_) owns the 16 scores of query head q_ for the tokens
-// 16 g_ .. 16 g_ + 15 (the same 16 channels of the value accumulator).
+// 32 k + 4 g_ + i (k, i = 0..3; the same 16 channels of the value accumulator).
 //
-// Operand layout.  A 4x4 byte transpose (8 byte permutes) turns word g_ of four
-// rows into four words, each holding byte j of the four rows; masking bit pair
-// i of every byte gives the A operand of code 4 j + i of four rows, scaled by
-// 4^i.  The scale is removed per output row in the fp32 epilogue.  Keys use
-// the factors (1, 4, 16, 16) for i = 0..3 (i = 3 shifted down by two bits) so
-// that the boosted high plane can reuse the same accumulators with its
-// factor 4 built into the masks ((4, 16, 64, 64) * high code).  The K index
-// (channels for keys, tokens for values) is permuted so that the 32 lanes'
-// word loads of a k-step hit 32 distinct banks; the fixed-point digit tables
-// are stored in the same permuted order.
+// Operand layout.  Both planes are stored with the packed dimension along a row
+// (key row = channel, 4 tokens per byte; value row = token, 4 channels per byte)
+// while the contraction runs along the rows, so a k-step loads 32 rows as two
+// transposed 16 x 16 byte matrices per half (ldmatrix .trans .b8): each lane gets,
+// for two row-bytes j, the bytes of 4 consecutive rows, and masking bit pair i of
+// every byte gives the A operand of element 4 j + i of those rows, scaled by 4^i.
+// The scale is removed per tile in the fp32 epilogue.  Keys use the factors
+// (1, 4, 16, 16) for i = 0..3 (i = 3 shifted down by two bits) so that the
+// boosted high plane can reuse the same accumulators with its factor 4 built into
+// the masks ((4, 16, 64, 64) * high code).  The fixed-point digit tables are
+// stored in natural K order with row and plane strides that keep their lane
+// loads on distinct banks.
 //
 // Reference semantics: (code - zp) * scale from kitty/kernels/dequantize_key.py:89-95
 // and kitty/kernels/quantize_value.py:121-133; softmax over [sinks ; pages ;
@@ -71,8 +73,8 @@ constexpr float kKeyRange = 4194300.0f;     // 2^22 - 4: |x| < 2^22 even with an
 constexpr float kValRange = 65535.0f;
 constexpr float kMagicKey = 12582912.0f;    // 1.5 * 2^23: fma(w, R, magic) has bits 0x4B400000 + rint(w R)
 constexpr float kMagicVal = 8388608.0f;     // 2^23: fma(P', Rv, magic) has bits 0x4B000000 + rint(P' Rv)
-constexpr int kPlane = 576;                 // digit table: plane stride (bytes)
-constexpr int kRow = 144;                   // digit table: query-head row stride (bytes)
+constexpr int kPlane = 656;                 // digit table: plane stride (bytes; 164 words = 4 mod 32 banks)
+constexpr int kRow = 160;                   // digit table: query-head row stride (bytes; 40 words = 8 mod 32)
 constexpr int kPhRow = 136;                 // fp16 P staging (fp16 region): row stride in halves
 
 // per-warp shared memory (bytes)
@@ -134,27 +136,20 @@ __device__ __forceinline__ float mul_f16_f32(uint16_t a, uint16_t b) {
   asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(0.0f));
   return d;
 }
-// 4x4 byte transpose: t[j] byte r = byte j of u[r]
-__device__ __forceinline__ void transpose4(const uint32_t (&u)[4], uint32_t (&t)[4]) {
-  const uint32_t a = prmt(u[0], u[1], 0x5140u), b = prmt(u[0], u[1], 0x7362u);
-  const uint32_t c = prmt(u[2], u[3], 0x5140u), d = prmt(u[2], u[3], 0x7362u);
-  t[0] = prmt(a, c, 0x5410u);
-  t[1] = prmt(a, c, 0x7632u);
-  t[2] = prmt(b, d, 0x5410u);
-  t[3] = prmt(b, d, 0x7632u);
+// Two transposed 16 x 16 byte matrices (rows from the addresses of lanes 0-15 and
+// 16-31): r[0] / r[1] = bytes 4 q_ .. 4 q_ + 3 of column g_ / g_ + 8 of the first
+// matrix, r[2] / r[3] the same of the second, i.e. the A operand of an m16n8k32
+// MMA whose K index is the matrix row.  The rows are written by bulk copies that
+// completed on an mbarrier wait (volatile keeps the load after it).
+__device__ __forceinline__ void ldsm_t_x2(uint32_t addr, uint32_t (&r)[4]) {
+  asm volatile("ldmatrix.sync.aligned.m16n16.x2.trans.shared.b8 {%0,%1,%2,%3}, [%4];\n"
+               : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+               : "r"(addr));
 }
 // code i of every byte of t, times the row factor (see the header comment)
 template <int i>
-__device__ __forceinline__ uint32_t key_code(uint32_t t) {
-  return i < 3 ? (t & (0x03030303u << (2 * i))) : ((t >> 2) & 0x30303030u);
-}
-template <int i>
 __device__ __forceinline__ uint32_t high_code(uint32_t t) {   // 4 * key_code factor
   return i < 3 ? ((t << 2) & (0x0C0C0C0Cu << (2 * i))) : (t & 0xC0C0C0C0u);
-}
-template <int i>
-__device__ __forceinline__ uint32_t val_code(uint32_t t) {
-  return t & (0x03030303u << (2 * i));
 }
 // bytes k of v0..v3 packed into one word
 __device__ __forceinline__ void bytes01(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t& w0,
@@ -172,62 +167,46 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
   memcpy(&h, &v, 4);
   return __half22float2(h);
 }
-// One 32-channel k-step of the key baseline plane (channels 32 ks + 16 hh + 4 kk + q_,
-// positions 32 ks + 16 hh + 4 q_ + kk) into the 8 token tiles.
+// One 32-channel k-step of the key baseline plane (K index = channel 32 ks + k) into
+// the 8 token tiles: tile 4 half + i, row r <-> token byte 16 half + r, code i, i.e.
+// token 64 half + 4 r + i.  lane_row = smem address of row 32 ks + lane of the plane.
 template <bool kFirst>
-__device__ __forceinline__ void key_kstep(int (&acc1)[8][4], int (&acc2)[8][4], const uint8_t* kbuf, const uint8_t* kb1,
-                                          const uint8_t* kb2, int ks, int g_, int q_) {
-  uint32_t u[4], v[4], t0[4], t1[4];
-  const uint8_t* r0 = kbuf + (32 * ks + q_) * 32 + 4 * g_;
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    u[kk] = lds32(r0 + kk * 4 * 32);
-    v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
-  }
-  transpose4(u, t0);
-  transpose4(v, t1);
+__device__ __forceinline__ void key_kstep(int (&acc1)[8][4], int (&acc2)[8][4], uint32_t lane_row,
+                                          const uint8_t* kb1, const uint8_t* kb2, int ks, int q_) {
   const uint32_t b10 = lds32(kb1 + 32 * ks + 4 * q_), b11 = lds32(kb1 + 32 * ks + 16 + 4 * q_);
   const uint32_t b20 = lds32(kb2 + 32 * ks + 4 * q_), b21 = lds32(kb2 + 32 * ks + 16 + 4 * q_);
 #pragma unroll
-  for (int jj = 0; jj < 4; ++jj) {
-    // tile 2 jj: tokens 4 jj + 0 (row g_) and 4 jj + 1 (row g_ + 8); tile 2 jj + 1: 4 jj + 2, 4 jj + 3
-    const uint32_t a00 = key_code<0>(t0[jj]), a01 = key_code<1>(t0[jj]);
-    const uint32_t a02 = key_code<0>(t1[jj]), a03 = key_code<1>(t1[jj]);
-    const uint32_t a10 = key_code<2>(t0[jj]), a11 = key_code<3>(t0[jj]);
-    const uint32_t a12 = key_code<2>(t1[jj]), a13 = key_code<3>(t1[jj]);
-    mma_k32_acc<kFirst>(acc1[2 * jj], a00, a01, a02, a03, b10, b11);
-    mma_k32_acc<kFirst>(acc1[2 * jj + 1], a10, a11, a12, a13, b10, b11);
-    mma_k32_acc<kFirst>(acc2[2 * jj], a00, a01, a02, a03, b20, b21);
-    mma_k32_acc<kFirst>(acc2[2 * jj + 1], a10, a11, a12, a13, b20, b21);
+  for (int half = 0; half < 2; ++half) {
+    uint32_t r[4];
+    ldsm_t_x2(lane_row + 16 * half, r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      // code i scaled by (1, 4, 16, 16)
+      const uint32_t m = i < 3 ? (0x03030303u << (2 * i)) : 0x30303030u;
+      const int sh = i < 3 ? 0 : 2;
+      const uint32_t c0 = (r[0] >> sh) & m, c1 = (r[1] >> sh) & m, c2 = (r[2] >> sh) & m, c3 = (r[3] >> sh) & m;
+      mma_k32_acc<kFirst>(acc1[4 * half + i], c0, c1, c2, c3, b10, b11);
+      mma_k32_acc<kFirst>(acc2[4 * half + i], c0, c1, c2, c3, b20, b21);
+    }
   }
 }
 
-// One 32-token k-step of the value plane (tokens 32 ks + 16 hh + 4 kk + q_) into the 8
-// channel tiles.
+// One 32-token k-step of the value plane (K index = token 32 ks + k) into the 8 channel
+// tiles: tile 4 half + i, row r <-> channel 64 half + 4 r + i.
 template <bool kFirst>
-__device__ __forceinline__ void val_kstep(int (&acc)[8][4], const uint8_t* vbuf, const uint8_t* vb, int ks, int g_,
-                                          int q_) {
-  uint32_t u[4], v[4], t0[4], t1[4];
-  const uint8_t* r0 = vbuf + (32 * ks + q_) * 32 + 4 * g_;
-#pragma unroll
-  for (int kk = 0; kk < 4; ++kk) {
-    u[kk] = lds32(r0 + kk * 4 * 32);
-    v[kk] = lds32(r0 + (16 + 4 * kk) * 32);
-  }
-  transpose4(u, t0);
-  transpose4(v, t1);
+__device__ __forceinline__ void val_kstep(int (&acc)[8][4], uint32_t lane_row, const uint8_t* vb, int ks, int q_) {
   const uint32_t b0 = lds32(vb + 32 * ks + 4 * q_), b1 = lds32(vb + 32 * ks + 16 + 4 * q_);
 #pragma unroll
-  for (int jj = 0; jj < 4; ++jj) {
-    mma_k32_acc<kFirst>(acc[2 * jj], val_code<0>(t0[jj]), val_code<1>(t0[jj]), val_code<0>(t1[jj]),
-                        val_code<1>(t1[jj]), b0, b1);
-    mma_k32_acc<kFirst>(acc[2 * jj + 1], val_code<2>(t0[jj]), val_code<3>(t0[jj]), val_code<2>(t1[jj]),
-                        val_code<3>(t1[jj]), b0, b1);
+  for (int half = 0; half < 2; ++half) {
+    uint32_t r[4];
+    ldsm_t_x2(lane_row + 16 * half, r);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const uint32_t m = 0x03030303u << (2 * i);
+      mma_k32_acc<kFirst>(acc[4 * half + i], r[0] & m, r[1] & m, r[2] & m, r[3] & m, b0, b1);
+    }
   }
 }
-
-// permuted K position of channel / token c (see the header comment)
-__device__ __forceinline__ int kpos(int c) { return (c & ~15) | ((c & 3) << 2) | ((c >> 2) & 3); }
 
 struct State {
   float o[16];   // unnormalised accumulator, channels 16 g_ + v, query head q_
@@ -305,7 +284,7 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
     const int r = bidx[c];
     const bool boosted = r < a.d_boost;
     const uint32_t bal = __ballot_sync(0xffffffffu, boosted);
-    if (boosted) ent[nb + __popc(bal & ((1u << lane) - 1u))] = uint32_t(r) * 32u | (uint32_t(kpos(c)) << 16);
+    if (boosted) ent[nb + __popc(bal & ((1u << lane) - 1u))] = uint32_t(r) * 32u | (uint32_t(c) << 16);
     nb += __popc(bal);
   }
   // pad to a multiple of 16 entries with the zero row
@@ -318,7 +297,8 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
 // Tokens [t_begin, t_end) of the fp16 region of (b, h) (sinks then tail; one chunk
 // item of the segment walk), at most 128 per pass (fp16 MMAs; 16-token tiles without
 // real tokens are skipped).  Scores: token 16 m + g_ + 8 hh <-> row g_ + 8 hh of M tile
-// m; values: channel 16 g_ + 2 m + hh <-> row g_ + 8 hh of M tile m.
+// m; values: channel 32 (m >> 1) + 4 g_ + 2 (m & 1) + hh <-> row g_ + 8 hh of M tile m
+// (the channels of st.o[2 m + hh], as on the page path).
 __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, State& st, uint8_t* wsm,
                                     const Layout& L, float qk_scale, int lane, int t_begin, int t_end) {
   const int cr = cache_row(a, b);   // cache row (sinks, tail, lengths)
@@ -399,23 +379,26 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
       }
     }
     __syncwarp();
-    // values: M = channels 16 g_ + 2 m (+1), K = tokens 16 k + (2q_, 2q_+1, 2q_+8, 2q_+9)
+    // values: M = channel pairs (word m of the lane's 8 words), K = tokens 16 k + (2q_,
+    // 2q_+1, 2q_+8, 2q_+9)
     float oacc[8][4];
 #pragma unroll
     for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
     const __half* pb = ph + (g_ >> 1) * kPhRow;
 #pragma unroll 1
     for (int k = 0; k < tiles; ++k) {
-      uint4 v[4][2];
+      uint2 v[4][4];   // token e, channels 32 j + 4 g_ .. + 3
       const int t0 = 16 * k + 2 * q_;
       const int ts[4] = {t0, t0 + 1, t0 + 8, t0 + 9};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
         if (ts[e] < ntok) {
-          const uint4* r = reinterpret_cast<const uint4*>(row(false, ts[e]) + 16 * g_);
-          v[e][0] = r[0]; v[e][1] = r[1];
+          const uint16_t* r = row(false, ts[e]) + 4 * g_;
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[e][j] = *reinterpret_cast<const uint2*>(r + 32 * j);
         } else {
-          v[e][0] = v[e][1] = make_uint4(0, 0, 0, 0);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) v[e][j] = make_uint2(0, 0);
         }
       }
       const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + t0);
@@ -517,6 +500,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   uint32_t qreg[8];
   int nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane, qreg);
 
+  // ldmatrix row addresses: row `lane` of a 32-row k-step of the key / value plane
+  const uint32_t k_row = smem_u32(kbuf) + 32u * lane, v_row = smem_u32(vbuf) + 32u * lane;
   // B operand bases: column g_ of an MMA = query head g_ >> 1, digit (g_ & 1 ? lo : hi)
   const uint8_t* kb1 = dtab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;   // b1 | b0
   const uint8_t* kb2 = dtab + ((g_ & 1) ? 3 : 2) * kPlane + (g_ >> 1) * kRow;   // b2 | ones
@@ -572,12 +557,12 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 2);
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 4);
-        // position word qq <-> channels 16 cb + qq + {0, 4, 8, 12}
+        // word qq <-> channels 16 cb + 4 qq .. 16 cb + 4 qq + 3
         uint32_t d0[4], d1[4], d2[4];
 #pragma unroll
         for (int qq = 0; qq < 4; ++qq) {
-          bytes01(fb[qq], fb[qq + 4], fb[qq + 8], fb[qq + 12], d0[qq], d1[qq]);
-          d2[qq] = byte2(fb[qq], fb[qq + 4], fb[qq + 8], fb[qq + 12]);
+          bytes01(fb[4 * qq], fb[4 * qq + 1], fb[4 * qq + 2], fb[4 * qq + 3], d0[qq], d1[qq]);
+          d2[qq] = byte2(fb[4 * qq], fb[4 * qq + 1], fb[4 * qq + 2], fb[4 * qq + 3]);
         }
         uint8_t* row = dtab + pq * kRow + 16 * cb;
         *reinterpret_cast<uint4*>(row) = make_uint4(d0[0], d0[1], d0[2], d0[3]);
@@ -591,30 +576,33 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 
       int acc1[8][4], acc2[8][4];
       // ---- baseline plane
-      key_kstep<true>(acc1, acc2, kbuf, kb1, kb2, 0, g_, q_);
+      key_kstep<true>(acc1, acc2, k_row, kb1, kb2, 0, q_);
 #pragma unroll 1
-      for (int ks = 1; ks < 4; ++ks) key_kstep<false>(acc1, acc2, kbuf, kb1, kb2, ks, g_, q_);
-      // ---- boosted high plane: K = entries 16 bs + 4 q_ + kk
+      for (int ks = 1; ks < 4; ++ks) key_kstep<false>(acc1, acc2, k_row + 1024u * ks, kb1, kb2, ks, q_);
+      // ---- boosted high plane: K = entries 16 bs + k (row of entry k from lane k,
+      // token bytes 0-15 / 16-31 as the two matrices of one transposed load)
       for (int bs = 0; bs < nb; bs += 16) {
         const uint4 e4 = *reinterpret_cast<const uint4*>(ent + bs + 4 * q_);
         const uint32_t es[4] = {e4.x, e4.y, e4.z, e4.w};
-        uint32_t u[4], t[4], bb1 = 0u, bb2 = 0u;
+        uint32_t r[4], bb1 = 0u, bb2 = 0u;
+        ldsm_t_x2(smem_u32(kh) + (ent[bs + (lane & 15)] & 0xffffu) + 16u * (lane >> 4), r);
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
-          u[kk] = lds32(kh + (es[kk] & 0xffffu) + 4 * g_);
           const uint32_t pos = es[kk] >> 16;
           bb1 |= uint32_t(kb1[pos]) << (8 * kk);
           bb2 |= uint32_t(kb2[pos]) << (8 * kk);
         }
-        transpose4(u, t);
 #pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const uint32_t a00 = high_code<0>(t[jj]), a01 = high_code<1>(t[jj]);
-          const uint32_t a10 = high_code<2>(t[jj]), a11 = high_code<3>(t[jj]);
-          mma_k16(acc1[2 * jj], a00, a01, bb1);
-          mma_k16(acc1[2 * jj + 1], a10, a11, bb1);
-          mma_k16(acc2[2 * jj], a00, a01, bb2);
-          mma_k16(acc2[2 * jj + 1], a10, a11, bb2);
+        for (int half = 0; half < 2; ++half) {
+          const uint32_t x0 = r[2 * half], x1 = r[2 * half + 1];
+          mma_k16(acc1[4 * half + 0], high_code<0>(x0), high_code<0>(x1), bb1);
+          mma_k16(acc2[4 * half + 0], high_code<0>(x0), high_code<0>(x1), bb2);
+          mma_k16(acc1[4 * half + 1], high_code<1>(x0), high_code<1>(x1), bb1);
+          mma_k16(acc2[4 * half + 1], high_code<1>(x0), high_code<1>(x1), bb2);
+          mma_k16(acc1[4 * half + 2], high_code<2>(x0), high_code<2>(x1), bb1);
+          mma_k16(acc2[4 * half + 2], high_code<2>(x0), high_code<2>(x1), bb2);
+          mma_k16(acc1[4 * half + 3], high_code<3>(x0), high_code<3>(x1), bb1);
+          mma_k16(acc2[4 * half + 3], high_code<3>(x0), high_code<3>(x1), bb2);
         }
       }
       __syncwarp();
@@ -622,20 +610,22 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       have_next = cursor_step(cur, a) && cursor_to_page(cur, a, f1);
       if (lane == 0 && have_next) issue_k(cur);
 
-      // ---- scores (log2 domain) of tokens 16 g_ + v, v = 2 m + hh
+      // ---- scores (log2 domain): s[4 k + i] <-> token 32 k + 4 g_ + i; tile 4 half + i
+      // holds tokens 64 half + 4 g_ + i (row g_, k = 2 half) and + 32 (row g_ + 8)
       float s[16];
       {
-        // row factors 1, 4, 16, 16 for token 2 m + hh: tiles with m even hold i = 0, 1, odd i = 2, 3
-        const float2 ce = make_float2(cq, cq * 0.25f), co = make_float2(cq * 0.0625f, cq * 0.0625f);
-        const float2 ce16 = make_float2(ce.x * 65536.0f, ce.y * 65536.0f), co16 = make_float2(co.x * 65536.0f, co.y * 65536.0f);
+        // row factors 1, 4, 16, 16 of code i
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const int lo0 = 256 * acc1[m][0] + acc1[m][1], lo1 = 256 * acc1[m][2] + acc1[m][3];
-          const int hi0 = acc2[m][0] - 64 * acc2[m][1], hi1 = acc2[m][2] - 64 * acc2[m][3];
-          const float2 t = fma2(make_float2(float(lo0), float(lo1)), (m & 1) ? co : ce, make_float2(-zq, -zq));
-          const float2 r = fma2(make_float2(float(hi0), float(hi1)), (m & 1) ? co16 : ce16, t);
-          s[2 * m] = r.x;
-          s[2 * m + 1] = r.y;
+        for (int mt = 0; mt < 8; ++mt) {
+          const int i = mt & 3, half = mt >> 2;
+          const float f = cq * (i == 0 ? 1.0f : i == 1 ? 0.25f : 0.0625f);
+          const float2 fl = make_float2(f, f), fh = make_float2(f * 65536.0f, f * 65536.0f);
+          const int lo0 = 256 * acc1[mt][0] + acc1[mt][1], lo1 = 256 * acc1[mt][2] + acc1[mt][3];
+          const int hi0 = acc2[mt][0] - 64 * acc2[mt][1], hi1 = acc2[mt][2] - 64 * acc2[mt][3];
+          const float2 t = fma2(make_float2(float(lo0), float(lo1)), fl, make_float2(-zq, -zq));
+          const float2 r = fma2(make_float2(float(hi0), float(hi1)), fh, t);
+          s[8 * half + i] = r.x;
+          s[8 * half + 4 + i] = r.y;
         }
       }
 
@@ -643,13 +633,12 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       v_phase ^= 1u;
       if (valid) {
         softmax_step(st, s);   // s -> p
-        // ---- P' = p * scale_v as 16-bit fixed point, tokens 16 g_ + v
-        const uint4* vm4 = reinterpret_cast<const uint4*>(vbuf + 4096 + 64 * g_);
+        // ---- P' = p * scale_v as 16-bit fixed point, tokens 32 k + 4 g_ + i (v = 4 k + i)
         uint32_t sz[16];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-          const uint4 x = vm4[i];
-          sz[4 * i] = x.x; sz[4 * i + 1] = x.y; sz[4 * i + 2] = x.z; sz[4 * i + 3] = x.w;
+        for (int k = 0; k < 4; ++k) {
+          const uint4 x = *reinterpret_cast<const uint4*>(vbuf + 4096 + 4 * (32 * k + 4 * g_));
+          sz[4 * k] = x.x; sz[4 * k + 1] = x.y; sz[4 * k + 2] = x.z; sz[4 * k + 3] = x.w;
         }
         float pp[16];
         float mp = 0.f;
@@ -680,27 +669,31 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         }
         const float zv = zv2.x + zv2.y;
         st.zs = __fmaf_rn(zv, dv, st.zs);
-        uint32_t y0[4], y1[4];
+        uint8_t* prow = ptab + q_ * kRow + 4 * g_;
 #pragma unroll
-        for (int qq = 0; qq < 4; ++qq) bytes01(yb[qq], yb[qq + 4], yb[qq + 8], yb[qq + 12], y0[qq], y1[qq]);
-        uint8_t* prow = ptab + q_ * kRow + 16 * g_;
-        *reinterpret_cast<uint4*>(prow) = make_uint4(y0[0], y0[1], y0[2], y0[3]);
-        *reinterpret_cast<uint4*>(prow + kPlane) = make_uint4(y1[0], y1[1], y1[2], y1[3]);
+        for (int k = 0; k < 4; ++k) {
+          uint32_t y0, y1;
+          bytes01(yb[4 * k], yb[4 * k + 1], yb[4 * k + 2], yb[4 * k + 3], y0, y1);
+          *reinterpret_cast<uint32_t*>(prow + 32 * k) = y0;
+          *reinterpret_cast<uint32_t*>(prow + kPlane + 32 * k) = y1;
+        }
         __syncwarp();
-        // ---- values: M = channels, K = tokens 32 ks + 16 hh + 4 kk + q_
+        // ---- values: M = channels, K = tokens 32 ks + k
         int acc[8][4];
-        val_kstep<true>(acc, vbuf, vb, 0, g_, q_);
+        val_kstep<true>(acc, v_row, vb, 0, q_);
 #pragma unroll 1
-        for (int ks = 1; ks < 4; ++ks) val_kstep<false>(acc, vbuf, vb, ks, g_, q_);
-        // ---- accumulate: channel 16 g_ + 2 m + hh, row factor 4^((2 m + hh) & 3)
-        const float2 ee = make_float2(dv, dv * 0.25f), eo = make_float2(dv * 0.0625f, dv * 0.015625f);
+        for (int ks = 1; ks < 4; ++ks) val_kstep<false>(acc, v_row + 1024u * ks, vb, ks, q_);
+        // ---- accumulate: tile 4 half + i holds channels 64 half + 4 g_ + i (row g_) and
+        // + 32 (row g_ + 8), i.e. st.o[8 half + i] and st.o[8 half + 4 + i]; row factor 4^i
 #pragma unroll
-        for (int m = 0; m < 8; ++m) {
-          const int c0 = 256 * acc[m][0] + acc[m][1], c1 = 256 * acc[m][2] + acc[m][3];
-          const float2 o = fma2(make_float2(float(c0), float(c1)), (m & 1) ? eo : ee,
-                                make_float2(st.o[2 * m], st.o[2 * m + 1]));
-          st.o[2 * m] = o.x;
-          st.o[2 * m + 1] = o.y;
+        for (int mt = 0; mt < 8; ++mt) {
+          const int i = mt & 3, half = mt >> 2;
+          const float f = dv * (i == 0 ? 1.0f : i == 1 ? 0.25f : i == 2 ? 0.0625f : 0.015625f);
+          const int c0 = 256 * acc[mt][0] + acc[mt][1], c1 = 256 * acc[mt][2] + acc[mt][3];
+          const float2 o = fma2(make_float2(float(c0), float(c1)), make_float2(f, f),
+                                make_float2(st.o[8 * half + i], st.o[8 * half + 4 + i]));
+          st.o[8 * half + i] = o.x;
+          st.o[8 * half + 4 + i] = o.y;
         }
       }
       __syncwarp();
@@ -720,10 +713,12 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       zs += __shfl_xor_sync(0xffffffffu, zs, 16);
       const int64_t base = ((int64_t(b) * H + h) * plan.num_splits + slot) * g;
       if (q_ < g) {
-        float4* o = reinterpret_cast<float4*>(plan.ws_o + (base + q_) * kD + 16 * g_);
+        // st.o[4 k + i] <-> channel 32 k + 4 g_ + i
+        float* o = plan.ws_o + (base + q_) * kD + 4 * g_;
 #pragma unroll
-        for (int i = 0; i < 4; ++i)
-          o[i] = make_float4(st.o[4 * i] - zs, st.o[4 * i + 1] - zs, st.o[4 * i + 2] - zs, st.o[4 * i + 3] - zs);
+        for (int k = 0; k < 4; ++k)
+          *reinterpret_cast<float4*>(o + 32 * k) =
+              make_float4(st.o[4 * k] - zs, st.o[4 * k + 1] - zs, st.o[4 * k + 2] - zs, st.o[4 * k + 3] - zs);
         if (g_ == 0) {
           plan.ws_m[base + q_] = st.m == -INFINITY ? -INFINITY : st.m * kLn2;
           plan.ws_l[base + q_] = l;
