@@ -577,7 +577,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       int acc1[8][4], acc2[8][4];
       // ---- baseline plane
       key_kstep<true>(acc1, acc2, k_row, kb1, kb2, 0, q_);
-#pragma unroll 1
+#pragma unroll
       for (int ks = 1; ks < 4; ++ks) key_kstep<false>(acc1, acc2, k_row + 1024u * ks, kb1, kb2, ks, q_);
       // ---- boosted high plane: K = entries 16 bs + k (row of entry k from lane k,
       // token bytes 0-15 / 16-31 as the two matrices of one transposed load)
@@ -681,7 +681,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         // ---- values: M = channels, K = tokens 32 ks + k
         int acc[8][4];
         val_kstep<true>(acc, v_row, vb, 0, q_);
-#pragma unroll 1
+#pragma unroll
         for (int ks = 1; ks < 4; ++ks) val_kstep<false>(acc, v_row + 1024u * ks, vb, ks, q_);
         // ---- accumulate: tile 4 half + i holds channels 64 half + 4 g_ + i (row g_) and
         // + 32 (row g_ + 8), i.e. st.o[8 half + i] and st.o[8 half + 4 + i]; row factor 4^i
