@@ -43,7 +43,7 @@ def test_key_page_functional(golden_npz, name):
 
 @pytest.mark.parametrize("name", KEY_CASES)
 def test_key_page_into_pool_views_and_dequant(golden_npz, name):
-    """Reference launcher signature writing into pool views (kitty/pipeline.py:537-546),
+    """Reference launcher signature writing into pool views (kitty/pipeline.py:214-230),
     with a transposed (non-contiguous) key source, then dequantise."""
     p = f"key/{name}/"
     K, sent = (int(x) for x in golden_npz[p + "params"])
@@ -80,7 +80,7 @@ def test_value_page_functional_and_views(golden_npz, name):
     G, D = v.shape
     vc = torch.zeros(2, 2, G, D // 4, dtype=torch.uint8, device=DEV)
     vm = torch.zeros(2, 2, G, 2, dtype=torch.float16, device=DEV)
-    # stride-2 metadata views, as the reference pipeline passes them (kitty/pipeline.py:561-566)
+    # stride-2 metadata views, as the reference pipeline passes them (kitty/pipeline.py:245-250)
     KK.quantize_value_page(cuda(v), vc[1][0], vm[1, 0, :, 0], vm[1, 0, :, 1])
     torch.cuda.synchronize()
     np.testing.assert_array_equal(vc[1, 0].cpu().numpy(), golden_npz[p + "codes"])
