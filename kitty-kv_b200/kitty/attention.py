@@ -3,8 +3,8 @@
 Same constructor, ``forward`` contract and factory as the reference
 (``kitty/attention.py:28-257``).  Decode (T == 1) pushes the token into the
 pipeline and runs the fused CUDA decode kernel over sinks + quantised pages +
-fp16 tail; prefill (T > 1) streams the tokens into the pipeline and returns
-causal SDPA over the raw fp16 K/V, as the reference does.
+fp16 tail; prefill (T > 1) appends the tokens to the pipeline in one bulk call
+and returns causal SDPA over the raw fp16 K/V, as the reference does.
 """
 
 from __future__ import annotations
@@ -64,9 +64,8 @@ class KittyPagedAttention(nn.Module):
         return out.unsqueeze(0).unsqueeze(2)
 
     def _prefill(self, q, k, v, seq_id: int) -> torch.Tensor:
-        T = q.shape[2]
-        for t in range(T):
-            self.pipeline.push_token(layer_id=self.layer_id, key=k[0, :, t, :], value=v[0, :, t, :], seq_id=seq_id)
+        # all T tokens in one call (full pages quantised straight from k / v)
+        self.pipeline.push_tokens(layer_id=self.layer_id, keys=k[0], values=v[0], seq_id=seq_id)
         k_exp = k.repeat_interleave(self.q_per_kv, dim=1)
         v_exp = v.repeat_interleave(self.q_per_kv, dim=1)
         return F.scaled_dot_product_attention(q, k_exp, v_exp, attn_mask=None, dropout_p=0.0,

@@ -128,6 +128,95 @@ class KittyInferencePipeline:
         if self._kq[l] == G:
             self._flush(l, seq_id)
 
+    def push_tokens(self, layer_id: int, keys: torch.Tensor, values: torch.Tensor, seq_id: int = 0) -> None:
+        """Append T tokens at once: keys / values (num_kv_heads, T, head_dim).
+
+        Same end state as T calls of :meth:`push_token` (buffers, counters, value
+        window, pages and their bytes).  With ``align_values=True`` every full group
+        of G tokens is quantised straight from ``keys`` / ``values`` in one launch per
+        tensor (the reference pushes a prefill token by token,
+        ``kitty/attention.py:169-177``); ``align_values=False`` keeps the per-token
+        path, whose value pages depend on the window's evictions token by token.
+        """
+        keys = keys.to(self._dtype).to(self.sink_k.device)
+        values = values.to(self._dtype).to(self.sink_v.device)
+        T = keys.shape[1]
+        if not self.align_values:
+            for t in range(T):
+                self.push_token(layer_id, keys[:, t], values[:, t], seq_id)
+            return
+        cfg = self.config
+        S, G = cfg.sink_size, cfg.q_buffer_size
+        l = layer_id
+        t = min(max(S - self._sink_fill[l], 0), T)
+        if t > 0:
+            f = self._sink_fill[l]
+            self.sink_k[l, :, f:f + t] = keys[:, :t]
+            self.sink_v[l, :, f:f + t] = values[:, :t]
+            self._sink_fill[l] += t
+        if t == T:
+            return
+        self._window_push(l, values[:, t:])
+        kq = self._kq[l]
+        if kq > 0:
+            pre = min(G - kq, T - t)
+            self.key_qbuf[l, :, kq:kq + pre] = keys[:, t:t + pre]
+            self.val_tail[l, :, kq:kq + pre] = values[:, t:t + pre]
+            self._kq[l] += pre
+            t += pre
+            if self._kq[l] == G:
+                self._flush_buffers(l, seq_id)
+        m = (T - t) // G
+        if m > 0:
+            keys_c, values_c = keys.contiguous(), values.contiguous()
+            dev = keys_c.device
+            pages = []
+            for _ in range(m):
+                page_num = self._page_counter[(seq_id, l)]
+                pages.append(self.layout.allocate_page(seq_id=seq_id, layer_id=l, page_number=page_num).physical_idx)
+                self._page_counter[(seq_id, l)] += 1
+            dst = torch.tensor(pages, dtype=torch.int32).to(dev, non_blocking=True)
+            offs = (torch.arange(m, dtype=torch.int64) * G + t) * keys_c.stride(1)
+            offs = offs.to(dev, non_blocking=True)
+            H, D, K = cfg.num_kv_heads, cfg.head_dim, cfg.d_boost
+            quantize_key_pages(keys_c, offs, (keys_c.stride(0), keys_c.stride(1), keys_c.stride(2)),
+                               self._boost_idx_dev()[l], K, cfg.sentinel, dst, self.layout.key_baseline,
+                               self.layout.key_boost, self.layout.key_metadata, H, D, G)
+            quantize_value_pages(values_c, offs, (values_c.stride(0), values_c.stride(1), values_c.stride(2)), dst,
+                                 self.layout.value_pool, self.layout.value_metadata, H, D, G)
+            t += m * G
+        rem = T - t
+        if rem > 0:
+            self.key_qbuf[l, :, :rem] = keys[:, t:]
+            self.val_tail[l, :, :rem] = values[:, t:]
+            self._kq[l] = rem
+
+    def _window_push(self, l: int, new_values: torch.Tensor) -> None:
+        """Value window (R most recent values) and Value Q-buffer after pushing the
+        (H, n, D) values one by one, with the Q-buffer emptied whenever the Key
+        Q-buffer reaches G tokens (push_token's bookkeeping, vectorised)."""
+        G, R = self.config.q_buffer_size, self.config.local_value_window
+        n = new_values.shape[1]
+        vl0, vq0, kq0 = self._vl[l], self._vq[l], self._kq[l]
+        W = torch.cat([self.val_local[l, :, :vl0], new_values], dim=1)   # oldest first
+        first = max(1, R - vl0 + 1)             # push index (1-based) of the first eviction
+        flushes = [p for p in range(1, n + 1) if (kq0 + p) % G == 0]
+        start = flushes[-1] + 1 if flushes else 1
+        lo = max(start, first)
+        ev = W[:, lo - first:n - first + 1] if n >= lo else W[:, :0]      # values evicted after the last flush
+        if flushes:
+            self.val_qbuf[l].zero_()
+            base = 0
+        else:
+            base = vq0
+        if ev.shape[1]:
+            self.val_qbuf[l, :, base:base + ev.shape[1]] = ev
+        self._vq[l] = base + ev.shape[1]
+        keep = min(R, vl0 + n)
+        if keep:
+            self.val_local[l, :, :keep] = W[:, W.shape[1] - keep:]
+        self._vl[l] = keep
+
     def _trigger_quantization(self, triggering_layer_id: int, seq_id: int) -> None:
         """Flush the Q-buffers of ``triggering_layer_id`` into a new page."""
         self._flush(triggering_layer_id, seq_id)
@@ -138,6 +227,13 @@ class KittyInferencePipeline:
         return self._bidx_dev
 
     def _flush(self, l: int, seq_id: int) -> None:
+        self._flush_buffers(l, seq_id)
+        self.val_qbuf[l].zero_()
+        self._vq[l] = 0
+
+    def _flush_buffers(self, l: int, seq_id: int) -> None:
+        """Quantise the Key Q-buffer and its value page into a new page; empty the
+        Key Q-buffer (and the aligned value tail)."""
         cfg = self.config
         G, H, D, K = cfg.q_buffer_size, cfg.num_kv_heads, cfg.head_dim, cfg.d_boost
         page_num = self._page_counter[(seq_id, l)]
@@ -159,8 +255,6 @@ class KittyInferencePipeline:
                              self.layout.value_pool, self.layout.value_metadata, H, D, G, n_valid=n_valid)
         self.key_qbuf[l].zero_()
         self._kq[l] = 0
-        self.val_qbuf[l].zero_()
-        self._vq[l] = 0
         if self.val_tail is not None:
             self.val_tail[l].zero_()
 

@@ -243,3 +243,76 @@ def test_profiler_compute_matches_oracle_rule():
     exp = np.stack([O.boost_idx_from_scores(np.abs(k).mean(axis=1), c.d_boost, c.sentinel) for k in keys])
     np.testing.assert_array_equal(prof.boost_idx_uint8.numpy(), exp)
     assert prof.boost_masks.sum().item() == 2 * 4 * c.d_boost
+
+
+class PageRecorder:
+    """Stands in for the quantise launches and materialises each job's (H, G, D) block
+    from (source, offsets, strides), so flushes from a buffer and pages quantised
+    straight from a prefill source can be compared."""
+
+    def __init__(self):
+        self.keys, self.values = {}, {}
+
+    @staticmethod
+    def _blocks(src, offs, strides, dst, H, D, G):
+        flat = src.reshape(-1) if src.is_contiguous() else src.contiguous().reshape(-1)
+        if not src.is_contiguous():
+            raise AssertionError("sources are passed contiguous")
+        sh, st, sc = strides
+        h = torch.arange(H).view(H, 1, 1) * sh
+        t = torch.arange(G).view(1, G, 1) * st
+        c = torch.arange(D).view(1, 1, D) * sc
+        return {int(p): flat[int(o) + h + t + c].clone() for o, p in zip(offs.tolist(), dst.tolist())}
+
+    def key(self, src, offs, strides, bidx, K, sent, dst, kl, kh, km, H, D, G):
+        self.keys.update(self._blocks(src, offs, strides, dst, H, D, G))
+
+    def value(self, src, offs, strides, dst, vc, vm, H, D, G, n_valid=None):
+        assert n_valid is None
+        self.values.update(self._blocks(src, offs, strides, dst, H, D, G))
+
+
+@pytest.mark.parametrize("R", [8, 3, 0])
+@pytest.mark.parametrize("chunks", [[1, 2, 30, 5], [4, 8, 8, 1], [17, 3, 0, 25], [2, 40]])
+def test_bulk_push_equals_token_by_token(monkeypatch, R, chunks):
+    """push_tokens (aligned values) leaves the same buffers, counters, value window,
+    value Q-buffer, page list and page contents as pushing the same tokens one by one."""
+    c = cfg(local_value_window=R)
+    H, D = c.num_kv_heads, c.head_dim
+    total = sum(chunks)
+    g = torch.Generator().manual_seed(R * 100 + total)
+    keys = torch.randn(H, total, D, generator=g).to(torch.float16)
+    vals = torch.randn(H, total, D, generator=g).to(torch.float16)
+    results = []
+    for bulk in (False, True):
+        rec = PageRecorder()
+        monkeypatch.setattr(pipeline_mod, "quantize_key_pages", rec.key)
+        monkeypatch.setattr(pipeline_mod, "quantize_value_pages", rec.value)
+        p, lay = make_pipe(c, True)
+        t = 0
+        for n in chunks:
+            if bulk:
+                p.push_tokens(0, keys[:, t:t + n], vals[:, t:t + n])
+            else:
+                for j in range(t, t + n):
+                    p.push_token(0, keys[:, j], vals[:, j])
+            t += n
+        results.append((p, lay, rec))
+    (a, la, ra), (b, lb, rb) = results
+    assert a.layer_state(0) == b.layer_state(0)
+    for name in ("sink_k", "sink_v", "key_qbuf", "val_tail", "val_local", "val_qbuf"):
+        assert torch.equal(getattr(a, name), getattr(b, name)), name
+    assert la.get_page_list(0, 0) == lb.get_page_list(0, 0)
+    assert ra.keys.keys() == rb.keys.keys() == set(la.get_page_list(0, 0))
+    for pg in ra.keys:
+        assert torch.equal(ra.keys[pg], rb.keys[pg]) and torch.equal(ra.values[pg], rb.values[pg])
+
+
+def test_bulk_push_reference_mode_goes_token_by_token(recorder):
+    c = cfg()
+    p, lay = make_pipe(c, align=False)
+    H, D = c.num_kv_heads, c.head_dim
+    n = c.sink_size + 2 * c.q_buffer_size + 3
+    p.push_tokens(0, torch.arange(n, dtype=torch.float16).view(1, n, 1).expand(H, n, D),
+                  (1000 + torch.arange(n, dtype=torch.float16)).view(1, n, 1).expand(H, n, D))
+    assert len(recorder.key_calls) == 2 and [cl["n_valid"] for cl in recorder.value_calls] == [0, c.q_buffer_size]
