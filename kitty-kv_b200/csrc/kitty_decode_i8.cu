@@ -17,7 +17,7 @@
 //           x is split into bytes: x = 65536 (b2 - 64) + 256 b1 + b0 (b0, b1, b2
 //           unsigned), so  sum_c code * x = 65536 (S[b2] - 64 S[1]) + 256 S[b1] + S[b0]
 //           where S[d] is the MMA sum against digit plane d and S[1] the code sum
-//           (an all-ones plane).  Scores = (sum_c code * x) / R - sum_c zp_k w,
+//           (an all-ones operand).  Scores = (sum_c code * x) / R - sum_c zp_k w,
 //           i.e. 23 significant bits per product (16 bits moved the logits by up
 //           to ~1e-3, too much next to the value outliers).
 //   values  P'[qh][t] = p[qh][t] * scale_v[t]           (fp32)
@@ -86,7 +86,7 @@ __host__ __device__ inline Layout i8_layout(int K) {
   int o = 0;
   L.kbuf = o; o += (4096 + 512 + K * 32 + 32 + 127) & ~127;  // low plane, scale/zero rows, high plane, zero row
   L.vbuf = o; o += 4096 + 512;                               // codes, (scale, zero) per token
-  L.dtab = o; o += 4 * kPlane;                               // key digits b0, b1, b2, ones [qh][channel]
+  L.dtab = o; o += 3 * kPlane;                               // key digits b0, b1, b2 [qh][channel]
   L.ptab = o; o += 2 * kPlane;                               // P' digits y0, y1 [qh][token] / fp16 P (fp16 region)
   L.ent = o;  o += 128 * 4;                                  // boosted entries (row offset | position << 16)
   L.bars = o; o += 16;
@@ -172,9 +172,10 @@ __device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
 // token 64 half + 4 r + i.  lane_row = smem address of row 32 ks + lane of the plane.
 template <bool kFirst>
 __device__ __forceinline__ void key_kstep(int (&acc1)[8][4], int (&acc2)[8][4], uint32_t lane_row,
-                                          const uint8_t* kb1, const uint8_t* kb2, int ks, int q_) {
+                                          const uint8_t* kb1, const uint8_t* kb2, bool ones, int ks, int q_) {
   const uint32_t b10 = lds32(kb1 + 32 * ks + 4 * q_), b11 = lds32(kb1 + 32 * ks + 16 + 4 * q_);
-  const uint32_t b20 = lds32(kb2 + 32 * ks + 4 * q_), b21 = lds32(kb2 + 32 * ks + 16 + 4 * q_);
+  const uint32_t b20 = ones ? 0x01010101u : lds32(kb2 + 32 * ks + 4 * q_);
+  const uint32_t b21 = ones ? 0x01010101u : lds32(kb2 + 32 * ks + 16 + 4 * q_);
 #pragma unroll
   for (int half = 0; half < 2; ++half) {
     uint32_t r[4];
@@ -458,8 +459,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     mbar_init(bar_v, 1);
   }
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
-  // constant tables: the all-ones digit plane and the zero row after the high plane
-  for (int i = lane; i < kPlane / 4; i += 32) reinterpret_cast<uint32_t*>(dtab + 3 * kPlane)[i] = 0x01010101u;
+  // constant table: the zero row after the high plane
   if (lane < 8) reinterpret_cast<uint32_t*>(kbuf + 4608 + K * 32)[lane] = 0u;
   __syncwarp();
 
@@ -504,7 +504,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   const uint32_t k_row = smem_u32(kbuf) + 32u * lane, v_row = smem_u32(vbuf) + 32u * lane;
   // B operand bases: column g_ of an MMA = query head g_ >> 1, digit (g_ & 1 ? lo : hi)
   const uint8_t* kb1 = dtab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;   // b1 | b0
-  const uint8_t* kb2 = dtab + ((g_ & 1) ? 3 : 2) * kPlane + (g_ >> 1) * kRow;   // b2 | ones
+  const uint8_t* kb2 = dtab + 2 * kPlane + (g_ >> 1) * kRow;                     // b2 (even columns)
+  const bool ones_col = (g_ & 1) != 0;                                          // odd columns: all-ones plane
   const uint8_t* vb = ptab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;    // y1 | y0
 
   for (int64_t f = f0; f < f1; ++f) {
@@ -576,9 +577,9 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 
       int acc1[8][4], acc2[8][4];
       // ---- baseline plane
-      key_kstep<true>(acc1, acc2, k_row, kb1, kb2, 0, q_);
+      key_kstep<true>(acc1, acc2, k_row, kb1, kb2, ones_col, 0, q_);
 #pragma unroll
-      for (int ks = 1; ks < 4; ++ks) key_kstep<false>(acc1, acc2, k_row + 1024u * ks, kb1, kb2, ks, q_);
+      for (int ks = 1; ks < 4; ++ks) key_kstep<false>(acc1, acc2, k_row + 1024u * ks, kb1, kb2, ones_col, ks, q_);
       // ---- boosted high plane: K = entries 16 bs + k (row of entry k from lane k,
       // token bytes 0-15 / 16-31 as the two matrices of one transposed load)
       for (int bs = 0; bs < nb; bs += 16) {
@@ -592,6 +593,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           bb1 |= uint32_t(kb1[pos]) << (8 * kk);
           bb2 |= uint32_t(kb2[pos]) << (8 * kk);
         }
+        if (ones_col) bb2 = 0x01010101u;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
           const uint32_t x0 = r[2 * half], x1 = r[2 * half + 1];
