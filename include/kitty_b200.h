@@ -19,7 +19,8 @@
  *   val_codes [P][H][G][D/4]  u8   2-bit value codes, byte j of token t holds
  *                                   channels 4j..4j+3
  *   val_meta  [P][H][G][2]    f16  per-token (scale, zero-point)
- * fp16 tensors are passed as their 16-bit patterns (uint16_t / void*).
+ * fp16 (or bf16, see KITTY_DTYPE_*) tensors are passed as their 16-bit
+ * patterns (uint16_t / void*); "f16" above means the call's 16-bit type.
  */
 #ifndef KITTY_B200_H_
 #define KITTY_B200_H_
@@ -37,7 +38,21 @@ extern "C" {
 #define KITTY_ERR_CUDA 3             /* a CUDA runtime call failed */
 #define KITTY_ERR_WORKSPACE 4        /* workspace missing or too small */
 
-#define KITTY_ABI_VERSION 2
+#define KITTY_ABI_VERSION 3
+
+/* 16-bit floating-point type of the fp16 tensors of a call (the `dtype` field
+ * of the argument structs; 0 = the zero-initialised default).  With bf16 the
+ * sources, buffers and metadata are bfloat16; quantisation keeps the
+ * reference's float32 arithmetic and stores scale and zero-point the way it
+ * does for a bfloat16 cache: rounded to fp16, then to bf16 (kitty/kernels/
+ * quantize_key.py:121-124 returns fp16 that the launcher copies into the bf16
+ * pool views, :261-269).  Decode outputs are fp16 in both cases (the
+ * reference's paged attention returns float16, kitty/kernels/attention.py:189). */
+#define KITTY_DTYPE_F16 0
+#define KITTY_DTYPE_BF16 1
+/* quantisers only: bf16 source, fp16 scale / zero-point (what the reference's
+ * functional quantize_*_page_torch returns for a bf16 input) */
+#define KITTY_DTYPE_BF16_F16META 3
 
 /* ABI version compiled into the library (KITTY_ABI_VERSION). */
 int kitty_abi_version(void);
@@ -85,6 +100,7 @@ typedef struct KittyKeyQuantArgs {
   int64_t high_s_page, high_s_head;
   int64_t meta_s_page, meta_s_head;
   int32_t n_jobs, num_heads, head_dim, group, d_boost, sentinel;
+  int32_t dtype;              /* KITTY_DTYPE_*: key source and key_scale / key_zero (BF16_F16META allowed) */
 } KittyKeyQuantArgs;
 
 int kitty_quantize_key_pages(const KittyKeyQuantArgs* args, void* stream);
@@ -111,6 +127,7 @@ typedef struct KittyValueQuantArgs {
   int64_t codes_s_page, codes_s_head;
   int64_t meta_s_page, meta_s_head, meta_s_tok;
   int32_t n_jobs, num_heads, head_dim, group;
+  int32_t dtype;              /* KITTY_DTYPE_*: value source and val_scale / val_zero (BF16_F16META allowed) */
 } KittyValueQuantArgs;
 
 int kitty_quantize_value_pages(const KittyValueQuantArgs* args, void* stream);
@@ -136,6 +153,7 @@ typedef struct KittyKeyDequantArgs {
   const int64_t* out_off;     /* [n_jobs] */
   int64_t out_s_ch, out_s_tok;
   int32_t n_jobs, num_heads, head_dim, group, d_boost;
+  int32_t dtype;              /* KITTY_DTYPE_*: key_scale / key_zero and out */
 } KittyKeyDequantArgs;
 
 int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream);
@@ -198,6 +216,7 @@ typedef struct KittyDecodeArgs {
    * subset of a KittyCacheState's sequences, in any order).  NULL = b.  Values
    * must be valid rows of those arrays. */
   const int32_t* seq_map;
+  int32_t dtype;                      /* KITTY_DTYPE_*: q, key_meta, val_meta, sinks, tail (out is fp16) */
 } KittyDecodeArgs;
 
 /* Bytes of workspace kitty_paged_decode needs; writes the split count it will
@@ -274,6 +293,7 @@ typedef struct KittyCacheState {
   int64_t* job_off;
   int32_t* job_page;
   int32_t* job_slot;
+  int32_t dtype;                      /* KITTY_DTYPE_*: buffers, appended rows and metadata */
 } KittyCacheState;
 
 /* Empty every sequence and put all pool pages on the free stack (pages are

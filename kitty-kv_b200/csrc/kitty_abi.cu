@@ -48,6 +48,8 @@ int validate_decode(const KittyDecodeArgs* a) {
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: sink length given without sink tensors");
   if ((a->tail_len || a->tail_len_all > 0) && (!a->tail_k || !a->tail_v))
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: tail length given without tail tensors");
+  if (a->dtype != KITTY_DTYPE_F16 && a->dtype != KITTY_DTYPE_BF16)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: dtype must be KITTY_DTYPE_F16 or KITTY_DTYPE_BF16");
   if (a->sink_len_all < 0 || a->tail_len_all < 0)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: negative region length");
   if (!simt_supports(*a) && !mma_supports(*a))

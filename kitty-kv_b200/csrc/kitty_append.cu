@@ -352,6 +352,8 @@ int validate_state(const KittyCacheState* st, const char* what) {
   if (st->max_seqs <= 0 || st->num_heads <= 0 || st->head_dim <= 0 || st->group <= 0 || st->sink_size < 0 ||
       st->max_pages_per_seq < 0 || st->pool_pages < 0 || st->d_boost < 0 || st->sentinel < 0)
     return fail(KITTY_ERR_INVALID_ARGUMENT, w + ": negative or zero size");
+  if (st->dtype != KITTY_DTYPE_F16 && st->dtype != KITTY_DTYPE_BF16)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, w + ": dtype must be KITTY_DTYPE_F16 or KITTY_DTYPE_BF16");
   if (st->pool_pages > 0x7fffffffLL)
     return fail(KITTY_ERR_INVALID_ARGUMENT, w + ": pool_pages must fit int32 page numbers");
   if (st->head_dim % 8 != 0 || st->group % 4 != 0)
@@ -408,6 +410,7 @@ int quantize_pages(const KittyCacheState& st, int n_jobs, const void* key, const
   ka.high_s_page = int64_t(H) * K * (G / 4); ka.high_s_head = int64_t(K) * (G / 4);
   ka.meta_s_page = int64_t(H) * 2 * D; ka.meta_s_head = 2 * D;
   ka.n_jobs = n_jobs; ka.num_heads = H; ka.head_dim = D; ka.group = G; ka.d_boost = K; ka.sentinel = st.sentinel;
+  ka.dtype = st.dtype;
   int rc = quantize_key_pages_impl(&ka, stream);
   if (rc != KITTY_OK) return rc;
   KittyValueQuantArgs va{};
@@ -420,6 +423,7 @@ int quantize_pages(const KittyCacheState& st, int n_jobs, const void* key, const
   va.codes_s_page = int64_t(H) * G * (D / 4); va.codes_s_head = int64_t(G) * (D / 4);
   va.meta_s_page = int64_t(H) * G * 2; va.meta_s_head = int64_t(G) * 2; va.meta_s_tok = 2;
   va.n_jobs = n_jobs; va.num_heads = H; va.head_dim = D; va.group = G;
+  va.dtype = st.dtype;
   return quantize_value_pages_impl(&va, stream);
 }
 

@@ -3,10 +3,12 @@
 // quantisers.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstring>
 #include <string>
 
 #include "../../include/kitty_b200.h"
@@ -56,5 +58,62 @@ __device__ __forceinline__ float h2f(uint16_t bits) {
 __device__ __forceinline__ uint16_t f2h(float x) {
   return __half_as_ushort(__float2half_rn(x));
 }
+
+// 16-bit float type of a call (KITTY_DTYPE_F16 / KITTY_DTYPE_BF16): conversions of
+// single values and packed pairs (low half first), NaN-propagating packed min / max,
+// and the metadata store.  Widening to float32 is exact for both types.
+template <bool kBf16>
+struct Half16;
+
+template <>
+struct Half16<false> {
+  static __device__ __forceinline__ float to_f(uint16_t x) { return __half2float(__ushort_as_half(x)); }
+  static __device__ __forceinline__ float2 to_f2(uint32_t x) {
+    __half2 h;
+    memcpy(&h, &x, 4);
+    return __half22float2(h);
+  }
+  static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
+    __half2 x, y;
+    memcpy(&x, &a, 4); memcpy(&y, &b, 4);
+    const __half2 r = __hmin2_nan(x, y);
+    uint32_t u; memcpy(&u, &r, 4); return u;
+  }
+  static __device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+    __half2 x, y;
+    memcpy(&x, &a, 4); memcpy(&y, &b, 4);
+    const __half2 r = __hmax2_nan(x, y);
+    uint32_t u; memcpy(&u, &r, 4); return u;
+  }
+  // scale / zero-point as stored by the reference: fp16 (RN)
+  static __device__ __forceinline__ uint16_t meta(float x) { return __half_as_ushort(__float2half_rn(x)); }
+  static __device__ __forceinline__ uint16_t from_f(float x) { return __half_as_ushort(__float2half_rn(x)); }
+};
+
+template <>
+struct Half16<true> {
+  static __device__ __forceinline__ float to_f(uint16_t x) { return __uint_as_float(uint32_t(x) << 16); }
+  static __device__ __forceinline__ float2 to_f2(uint32_t x) {
+    return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
+  }
+  static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
+    __nv_bfloat162 x, y;
+    memcpy(&x, &a, 4); memcpy(&y, &b, 4);
+    const __nv_bfloat162 r = __hmin2_nan(x, y);
+    uint32_t u; memcpy(&u, &r, 4); return u;
+  }
+  static __device__ __forceinline__ uint32_t max2(uint32_t a, uint32_t b) {
+    __nv_bfloat162 x, y;
+    memcpy(&x, &a, 4); memcpy(&y, &b, 4);
+    const __nv_bfloat162 r = __hmax2_nan(x, y);
+    uint32_t u; memcpy(&u, &r, 4); return u;
+  }
+  // the reference returns fp16 scale / zero-point and copies them into the bf16
+  // pool: fp16 (RN), then bf16 (RN)
+  static __device__ __forceinline__ uint16_t meta(float x) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(__half2float(__float2half_rn(x))));
+  }
+  static __device__ __forceinline__ uint16_t from_f(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+};
 
 }  // namespace kitty

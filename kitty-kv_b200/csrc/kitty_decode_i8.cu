@@ -130,8 +130,23 @@ __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1,
       : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
       : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
 }
-// exact product of two fp16 values in fp32
-__device__ __forceinline__ float mul_f16_f32(uint16_t a, uint16_t b) {
+__device__ __forceinline__ void mma_bf16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+template <bool kBf16>
+__device__ __forceinline__ void mma_h16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3, uint32_t b0,
+                                        uint32_t b1) {
+  if (kBf16) mma_bf16(c, a0, a1, a2, a3, b0, b1);
+  else mma_f16(c, a0, a1, a2, a3, b0, b1);
+}
+// exact product of two 16-bit floats in fp32 (11- or 8-bit significands)
+template <bool kBf16>
+__device__ __forceinline__ float mul_h16_f32(uint16_t a, uint16_t b) {
+  if (kBf16) return Half16<true>::to_f(a) * Half16<true>::to_f(b);
   float d;
   asm("fma.rn.f32.f16 %0, %1, %2, %3;" : "=f"(d) : "h"(a), "h"(b), "f"(0.0f));
   return d;
@@ -161,12 +176,7 @@ __device__ __forceinline__ void bytes01(uint32_t v0, uint32_t v1, uint32_t v2, u
 __device__ __forceinline__ uint32_t byte2(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
   return prmt(prmt(v0, v1, 0x0062u), prmt(v2, v3, 0x0062u), 0x5410u);
 }
-// fp16 pair (low half first) -> float2
-__device__ __forceinline__ float2 h2_to_f2(uint32_t v) {
-  __half2 h;
-  memcpy(&h, &v, 4);
-  return __half22float2(h);
-}
+
 // One 32-channel k-step of the key baseline plane (K index = channel 32 ks + k) into
 // the 8 token tiles: tile 4 half + i, row r <-> token byte 16 half + r, code i, i.e.
 // token 64 half + 4 r + i.  lane_row = smem address of row 32 ks + lane of the plane.
@@ -300,6 +310,7 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
 // real tokens are skipped).  Scores: token 16 m + g_ + 8 hh <-> row g_ + 8 hh of M tile
 // m; values: channel 32 (m >> 1) + 4 g_ + 2 (m & 1) + hh <-> row g_ + 8 hh of M tile m
 // (the channels of st.o[2 m + hh], as on the page path).
+template <bool kBf16>
 __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, State& st, uint8_t* wsm,
                                     const Layout& L, float qk_scale, int lane, int t_begin, int t_end) {
   const int cr = cache_row(a, b);   // cache row (sinks, tail, lengths)
@@ -364,19 +375,29 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
         const uint32_t* wb = reinterpret_cast<const uint32_t*>(kb);
 #pragma unroll
         for (int k = 0; k < 8; ++k)
-          mma_f16(acc, wa[2 * k], wb[2 * k], wa[2 * k + 1], wb[2 * k + 1], qw[2 * k], qw[2 * k + 1]);
+          mma_h16<kBf16>(acc, wa[2 * k], wb[2 * k], wa[2 * k + 1], wb[2 * k + 1], qw[2 * k], qw[2 * k + 1]);
         if (ta < ntok) s[2 * m] = acc[0] * qk_scale;
         if (tb < ntok) s[2 * m + 1] = acc[2] * qk_scale;
       }
     }
     softmax_step(st, s);
-    // P (scale 1) as fp16 [query head q_][token]; tokens past ntok hold zeros
+    // P (scale 1) as fp16 [query head q_][token]; tokens past ntok hold zeros.  For bf16
+    // values P is carried as two bf16 parts (hi + lo, 16 significant bits), the lo part in
+    // the key digit table (unused on this path)
     {
-      __half* prow = ph + q_ * kPhRow;
+      uint16_t* prow = reinterpret_cast<uint16_t*>(ph) + q_ * kPhRow;
+      uint16_t* plo = reinterpret_cast<uint16_t*>(wsm + L.dtab) + q_ * kPhRow;
 #pragma unroll
-      for (int m = 0; m < 8; ++m) {
-        prow[16 * m + g_] = __float2half_rn(s[2 * m]);
-        prow[16 * m + g_ + 8] = __float2half_rn(s[2 * m + 1]);
+      for (int m = 0; m < 16; ++m) {
+        const int t = 16 * (m >> 1) + g_ + 8 * (m & 1);
+        const float p = s[m];
+        if (kBf16) {
+          const __nv_bfloat16 hi = __float2bfloat16_rn(p);
+          prow[t] = __bfloat16_as_ushort(hi);
+          plo[t] = __bfloat16_as_ushort(__float2bfloat16_rn(p - __bfloat162float(hi)));
+        } else {
+          prow[t] = __half_as_ushort(__float2half_rn(p));
+        }
       }
     }
     __syncwarp();
@@ -386,6 +407,7 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
 #pragma unroll
     for (int m = 0; m < 8; ++m) oacc[m][0] = oacc[m][1] = oacc[m][2] = oacc[m][3] = 0.f;
     const __half* pb = ph + (g_ >> 1) * kPhRow;
+    const __half* pbl = reinterpret_cast<const __half*>(wsm + L.dtab) + (g_ >> 1) * kPhRow;
 #pragma unroll 1
     for (int k = 0; k < tiles; ++k) {
       uint2 v[4][4];   // token e, channels 32 j + 4 g_ .. + 3
@@ -404,14 +426,18 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
       }
       const uint32_t b0 = *reinterpret_cast<const uint32_t*>(pb + t0);
       const uint32_t b1 = *reinterpret_cast<const uint32_t*>(pb + t0 + 8);
+      const uint32_t b0l = kBf16 ? *reinterpret_cast<const uint32_t*>(pbl + t0) : 0u;
+      const uint32_t b1l = kBf16 ? *reinterpret_cast<const uint32_t*>(pbl + t0 + 8) : 0u;
       const uint32_t* w0 = reinterpret_cast<const uint32_t*>(v[0]);
       const uint32_t* w1 = reinterpret_cast<const uint32_t*>(v[1]);
       const uint32_t* w2 = reinterpret_cast<const uint32_t*>(v[2]);
       const uint32_t* w3 = reinterpret_cast<const uint32_t*>(v[3]);
 #pragma unroll
       for (int m = 0; m < 8; ++m) {
-        mma_f16(oacc[m], prmt(w0[m], w1[m], 0x5410u), prmt(w0[m], w1[m], 0x7632u), prmt(w2[m], w3[m], 0x5410u),
-                prmt(w2[m], w3[m], 0x7632u), b0, b1);
+        const uint32_t a0 = prmt(w0[m], w1[m], 0x5410u), a1 = prmt(w0[m], w1[m], 0x7632u);
+        const uint32_t a2 = prmt(w2[m], w3[m], 0x5410u), a3 = prmt(w2[m], w3[m], 0x7632u);
+        mma_h16<kBf16>(oacc[m], a0, a1, a2, a3, b0, b1);
+        if (kBf16) mma_bf16(oacc[m], a0, a1, a2, a3, b0l, b1l);
       }
     }
 #pragma unroll
@@ -423,8 +449,10 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
   }
 }
 
+template <bool kBf16>
 __global__ void __launch_bounds__(kThreads, kCtasPerSm)
 decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+  using T = Half16<kBf16>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.d_boost, H = a.num_kv_heads, B = a.batch;
   const int g = a.num_q_heads / H;
@@ -513,7 +541,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (pos.p < pos.n16) {
       int t0, t1;
       fp16_chunk(fp16_tokens(a, pos.s), pos.n16, pos.p, t0, t1);
-      process_fp16_region(a, b, h, g, st, wsm, L, qk_scale, lane, t0, t1);
+      process_fp16_region<kBf16>(a, b, h, g, st, wsm, L, qk_scale, lane, t0, t1);
     } else {
       const int64_t page = phys(pos.s, pos.p, pos.n16);
       const bool valid = page >= 0 && page < a.pool_pages;
@@ -535,8 +563,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         float mx = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          w[2 * j] = mul_f16_f32(uint16_t(qreg[j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
-          w[2 * j + 1] = mul_f16_f32(uint16_t(qreg[j] >> 16), uint16_t(sw[j] >> 16));
+          w[2 * j] = mul_h16_f32<kBf16>(uint16_t(qreg[j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
+          w[2 * j + 1] = mul_h16_f32<kBf16>(uint16_t(qreg[j] >> 16), uint16_t(sw[j] >> 16));
           mx = fmaxf(mx, fmaxf(fabsf(w[2 * j]), fabsf(w[2 * j + 1])));
         }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -552,7 +580,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           const float2 f = fma2(wj, make_float2(R, R), make_float2(kMagicKey, kMagicKey));
           fb[2 * j] = __float_as_uint(f.x);
           fb[2 * j + 1] = __float_as_uint(f.y);
-          zs2 = fma2(h2_to_f2(zw[j]), wj, zs2);
+          zs2 = fma2(T::to_f2(zw[j]), wj, zs2);
         }
         zsum = zs2.x + zs2.y;
         zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
@@ -647,7 +675,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 #pragma unroll
         for (int v = 0; v < 16; v += 2) {
           // (scale, zero) of tokens v and v + 1 -> (scale_v, scale_v+1)
-          const float2 sc = h2_to_f2(prmt(sz[v], sz[v + 1], 0x5410u));
+          const float2 sc = T::to_f2(prmt(sz[v], sz[v + 1], 0x5410u));
           const float2 pr = mul2(make_float2(s[v], s[v + 1]), sc);
           pp[v] = pr.x;
           pp[v + 1] = pr.y;
@@ -667,7 +695,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           yb[v + 1] = __float_as_uint(fy.y);
           const float2 y = add2(fy, make_float2(-kMagicVal, -kMagicVal));
           const uint32_t zz = prmt(sz[v], sz[v + 1], 0x7632u);   // zero-points of tokens v, v + 1
-          zv2 = fma2(h2_to_f2(zz), y, zv2);
+          zv2 = fma2(T::to_f2(zz), y, zv2);
         }
         const float zv = zv2.x + zv2.y;
         st.zs = __fmaf_rn(zv, dv, st.zs);
@@ -785,12 +813,14 @@ void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   plan->grid = int(std::max<int64_t>(1, ctas));
 }
 
-int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
-  const Layout L = i8_layout(a.d_boost);
-  const int smem = kWarps * L.size;
+namespace {
+// shared-memory attribute and resident CTAs per SM of one instantiation, set up once
+// per shared-memory size
+template <bool kBf16>
+int prepare_i8(int smem, int* blocks) {
   static int configured_bytes = 0;
   if (configured_bytes < smem) {
-    cudaError_t e = cudaFuncSetAttribute(decode_i8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e = cudaFuncSetAttribute(decode_i8_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(KITTY_ERR_CUDA, std::string("decode_i8 smem attribute: ") + cudaGetErrorString(e));
     configured_bytes = smem;
   }
@@ -798,20 +828,34 @@ int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStrea
   static int occ_smem = -1, occ_blocks = kCtasPerSm;
   if (occ_smem != smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel, kThreads, smem) != cudaSuccess || n <= 0) {
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16>, kThreads, smem) != cudaSuccess ||
+        n <= 0) {
       cudaGetLastError();
       n = 1;
     }
     occ_blocks = std::min(n, kCtasPerSm);
     occ_smem = smem;
   }
+  *blocks = occ_blocks;
+  return KITTY_OK;
+}
+}  // namespace
+
+int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
+  const Layout L = i8_layout(a.d_boost);
+  const int smem = kWarps * L.size;
+  const bool bf16 = a.dtype == KITTY_DTYPE_BF16;
+  int occ_blocks = 1;
+  const int rc = bf16 ? prepare_i8<true>(smem, &occ_blocks) : prepare_i8<false>(smem, &occ_blocks);
+  if (rc != KITTY_OK) return rc;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
     cudaGetLastError();
     sms = 148;
   }
   const int grid = std::max(1, std::min(plan.grid, sms * occ_blocks));
-  decode_i8_kernel<<<grid, kThreads, smem, stream>>>(a, plan);
+  if (bf16) decode_i8_kernel<true><<<grid, kThreads, smem, stream>>>(a, plan);
+  else decode_i8_kernel<false><<<grid, kThreads, smem, stream>>>(a, plan);
   return check_launch("decode_i8_kernel");
 }
 

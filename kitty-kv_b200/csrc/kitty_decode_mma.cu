@@ -584,6 +584,7 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 }  // namespace
 
 bool mma_supports(const KittyDecodeArgs& a) {
+  if (a.dtype != KITTY_DTYPE_F16) return false;   // fp16 operands only
   const int g = a.num_q_heads / a.num_kv_heads;
   auto region_ok = [](const void* p, int64_t s_seq, int64_t s_head, int64_t s_tok) {
     return p == nullptr || (aligned(p, 16) && s_seq % 8 == 0 && s_head % 8 == 0 && s_tok % 8 == 0);

@@ -45,8 +45,10 @@ __host__ __device__ inline SimtSmem simt_layout(int D, int G, int K, int g) {
   return s;
 }
 
+template <bool kBf16>
 __global__ void __launch_bounds__(kSimtThreads)
 decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+  using T = Half16<kBf16>;
   extern __shared__ __align__(16) uint8_t smem[];
   const int D = a.head_dim, G = a.group, K = a.d_boost, H = a.num_kv_heads;
   const int g = a.num_q_heads / H;
@@ -72,7 +74,7 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   const uint16_t* qg = reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq + (h * g) * a.q_s_head;
   for (int i = tid; i < g * D; i += kSimtThreads) {
     const int qh = i / D, c = i - qh * D;
-    q_s[i] = h2f(qg[qh * a.q_s_head + c]);
+    q_s[i] = T::to_f(qg[qh * a.q_s_head + c]);
   }
   const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
   for (int c = tid; c < D; c += kSimtThreads) {
@@ -138,7 +140,7 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
             uint32_t code = (kl_s[c * G4 + j] >> sh) & 3u;
             const int r = row_s[c];
             if (r >= 0) code |= ((kh_s[r * G4 + j] >> sh) & 3u) << 2;
-            const float kv = (static_cast<float>(code) - h2f(km_s[D + c])) * h2f(km_s[c]);
+            const float kv = (static_cast<float>(code) - T::to_f(km_s[D + c])) * T::to_f(km_s[c]);
 #pragma unroll
             for (int qh = 0; qh < kMaxGroupSimt; ++qh)
               if (qh < g) acc[qh] = fmaf(q_s[qh * D + c], kv, acc[qh]);
@@ -149,7 +151,7 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
               ? reinterpret_cast<const uint16_t*>(a.sink_k) + cr * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
               : reinterpret_cast<const uint16_t*>(a.tail_k) + cr * a.tk_s_seq + h * a.tk_s_head + (ft - sink_len) * a.tk_s_tok;
           for (int c = 0; c < D; ++c) {
-            const float kv = h2f(kp[c]);
+            const float kv = T::to_f(kp[c]);
 #pragma unroll
             for (int qh = 0; qh < kMaxGroupSimt; ++qh)
               if (qh < g) acc[qh] = fmaf(q_s[qh * D + c], kv, acc[qh]);
@@ -210,7 +212,7 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         const int D4 = D / 4, jj = c >> 2, sh = 2 * (c & 3);
         for (int t = 0; t < ntok; ++t) {
           const uint32_t code = (vc_s[t * D4 + jj] >> sh) & 3u;
-          const float vv = (static_cast<float>(code) - h2f(vm_s[2 * t + 1])) * h2f(vm_s[2 * t]);
+          const float vv = (static_cast<float>(code) - T::to_f(vm_s[2 * t + 1])) * T::to_f(vm_s[2 * t]);
 #pragma unroll
           for (int qh = 0; qh < kMaxGroupSimt; ++qh)
             if (qh < g) acc[qh] = fmaf(p_s[qh * chunk_cap + t], vv, acc[qh]);
@@ -221,7 +223,7 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           const uint16_t* vp = (ft < sink_len)
               ? reinterpret_cast<const uint16_t*>(a.sink_v) + cr * a.sv_s_seq + h * a.sv_s_head + ft * a.sv_s_tok
               : reinterpret_cast<const uint16_t*>(a.tail_v) + cr * a.tv_s_seq + h * a.tv_s_head + (ft - sink_len) * a.tv_s_tok;
-          const float vv = h2f(vp[c]);
+          const float vv = T::to_f(vp[c]);
 #pragma unroll
           for (int qh = 0; qh < kMaxGroupSimt; ++qh)
             if (qh < g) acc[qh] = fmaf(p_s[qh * chunk_cap + t], vv, acc[qh]);
@@ -334,10 +336,13 @@ int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStr
   const int g = a.num_q_heads / a.num_kv_heads;
   const SimtSmem L = simt_layout(a.head_dim, a.group, a.d_boost, g);
   if (L.total > 200 * 1024) return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: shape needs too much shared memory");
-  if (L.total > 48 * 1024)
-    cudaFuncSetAttribute(decode_simt_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+  if (L.total > 48 * 1024) {
+    cudaFuncSetAttribute(decode_simt_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+    cudaFuncSetAttribute(decode_simt_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
+  }
   dim3 grid(plan.num_splits, a.num_kv_heads, a.batch);
-  decode_simt_kernel<<<grid, kSimtThreads, L.total, stream>>>(a, plan);
+  if (a.dtype == KITTY_DTYPE_BF16) decode_simt_kernel<true><<<grid, kSimtThreads, L.total, stream>>>(a, plan);
+  else decode_simt_kernel<false><<<grid, kSimtThreads, L.total, stream>>>(a, plan);
   return check_launch("decode_simt_kernel");
 }
 

@@ -5,7 +5,9 @@
 // IEEE float32 (kitty/kernels/quantize_key.py:69-124,
 // kitty/kernels/quantize_value.py:50-90): divisions are correctly rounded
 // (__fdiv_rn), rounding is half-to-even (rintf), and the stored scale is the
-// float32 scale rounded to fp16.  The packed planes are therefore bit-exact.
+// float32 scale rounded to fp16 (then to bf16 for a bfloat16 cache, as the
+// reference's copy into bf16 pool views does).  The packed planes are therefore
+// bit-exact.  Every kernel is instantiated for fp16 and bf16 sources (Half16).
 //
 // One CTA handles one page-head.  The general kernels stage the G x D fp16
 // block in shared memory, reduce per channel (keys) or per token (values),
@@ -46,8 +48,10 @@ __device__ __forceinline__ void stage_block(uint16_t* tile, const uint16_t* src,
   }
 }
 
+template <bool kBf16, bool kMetaBf16>
 __global__ void __launch_bounds__(kQuantThreads)
 quantize_key_kernel(const KittyKeyQuantArgs a) {
+  using T = Half16<kBf16>;
   extern __shared__ __align__(16) uint8_t smem[];
   const int D = a.head_dim, G = a.group, K = a.d_boost;
   const int job = blockIdx.x / a.num_heads;
@@ -76,9 +80,9 @@ quantize_key_kernel(const KittyKeyQuantArgs a) {
 
   // Per-channel statistics (quantize_key.py:73-87).
   for (int c = threadIdx.x; c < D; c += blockDim.x) {
-    float mn = h2f(tile[c]), mx = mn;
+    float mn = T::to_f(tile[c]), mx = mn;
     for (int t = 1; t < G; ++t) {
-      const float x = h2f(tile[t * D + c]);
+      const float x = T::to_f(tile[t * D + c]);
       mn = tmin(mn, x);
       mx = tmax(mx, x);
     }
@@ -93,8 +97,8 @@ quantize_key_kernel(const KittyKeyQuantArgs a) {
     s_zp[c] = zp;
     s_maxq[c] = maxq;
     s_row[c] = (boosted && b < K) ? b : -1;
-    out_scale[c] = f2h(scale);
-    out_zero[c] = f2h(zp);
+    out_scale[c] = Half16<kMetaBf16>::meta(scale);
+    out_zero[c] = Half16<kMetaBf16>::meta(zp);
   }
   __syncthreads();
 
@@ -107,7 +111,7 @@ quantize_key_kernel(const KittyKeyQuantArgs a) {
     uint32_t low = 0u, high = 0u;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float x = h2f(tile[(4 * j + k) * D + c]);
+      const float x = T::to_f(tile[(4 * j + k) * D + c]);
       float q = rintf(__fdiv_rn(x, scale)) + zp;
       q = tmin(tmax(q, 0.0f), maxq);
       const uint32_t code = to_code(q);
@@ -128,8 +132,10 @@ quantize_key_kernel(const KittyKeyQuantArgs a) {
   for (int i = threadIdx.x; i < K * G4; i += blockDim.x) out_high[i] = sh[i];
 }
 
+template <bool kBf16, bool kMetaBf16>
 __global__ void __launch_bounds__(kQuantThreads)
 quantize_value_kernel(const KittyValueQuantArgs a) {
+  using T = Half16<kBf16>;
   extern __shared__ __align__(16) uint8_t smem[];
   const int D = a.head_dim, G = a.group;
   const int job = blockIdx.x / a.num_heads;
@@ -153,9 +159,9 @@ quantize_value_kernel(const KittyValueQuantArgs a) {
   // Per-token statistics (quantize_value.py:62-72): a warp per token, lanes over channels.
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nwarps = blockDim.x >> 5;
   for (int t = warp; t < G; t += nwarps) {
-    float mn = h2f(tile[t * D + (lane < D ? lane : 0)]), mx = mn;
+    float mn = T::to_f(tile[t * D + (lane < D ? lane : 0)]), mx = mn;
     for (int c = lane + 32; c < D; c += 32) {
-      const float x = h2f(tile[t * D + c]);
+      const float x = T::to_f(tile[t * D + c]);
       mn = tmin(mn, x);
       mx = tmax(mx, x);
     }
@@ -171,8 +177,8 @@ quantize_value_kernel(const KittyValueQuantArgs a) {
       zp = tmin(tmax(zp, 0.0f), 3.0f);
       s_scale[t] = scale;
       s_zp[t] = zp;
-      out_scale[t * a.meta_s_tok] = f2h(scale);
-      out_zero[t * a.meta_s_tok] = f2h(zp);
+      out_scale[t * a.meta_s_tok] = Half16<kMetaBf16>::meta(scale);
+      out_zero[t * a.meta_s_tok] = Half16<kMetaBf16>::meta(zp);
     }
   }
   __syncthreads();
@@ -186,7 +192,7 @@ quantize_value_kernel(const KittyValueQuantArgs a) {
     uint32_t byte = 0u;
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
-      const float x = h2f(tile[t * D + 4 * j + k]);
+      const float x = T::to_f(tile[t * D + 4 * j + k]);
       float q = rintf(__fdiv_rn(x, scale)) + zp;
       q = tmin(tmax(q, 0.0f), 3.0f);
       byte |= (to_code(q) & 3u) << (2 * k);
@@ -195,7 +201,9 @@ quantize_value_kernel(const KittyValueQuantArgs a) {
   }
 }
 
+template <bool kBf16>
 __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
+  using T = Half16<kBf16>;
   const int D = a.head_dim, G = a.group, K = a.d_boost, G4 = G / 4;
   const int job = blockIdx.x;
   const int64_t page = a.src_page[job];
@@ -213,12 +221,12 @@ __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
     const int b = bidx[c];
     const uint32_t lo = low[i];
     const uint32_t hi = (b < K) ? high[b * G4 + j] : 0u;
-    const float s = h2f(sc[c]), z = h2f(zr[c]);
+    const float s = T::to_f(sc[c]), z = T::to_f(zr[c]);
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t code = ((lo >> (2 * k)) & 3u) | (((hi >> (2 * k)) & 3u) << 2);
       const float x = (static_cast<float>(code) - z) * s;
-      out[c * a.out_s_ch + (4 * j + k) * a.out_s_tok] = f2h(x);
+      out[c * a.out_s_ch + (4 * j + k) * a.out_s_tok] = T::from_f(x);
     }
   }
 }
@@ -262,9 +270,6 @@ __device__ __forceinline__ void load_tile(Tile8x8& t, const uint16_t* src, int64
   }
 }
 
-__device__ __forceinline__ __half2 u2h2(uint32_t x) { return *reinterpret_cast<__half2*>(&x); }
-__device__ __forceinline__ uint32_t h22u(__half2 x) { return *reinterpret_cast<uint32_t*>(&x); }
-
 __device__ __forceinline__ uint32_t word_of(const uint4& v, int w) {
   return w == 0 ? v.x : w == 1 ? v.y : w == 2 ? v.z : v.w;
 }
@@ -287,9 +292,10 @@ __device__ __forceinline__ uint32_t quant_code(float x, float scale, float zp, f
 // with the exact division by the caller.  The clamp to [0, maxq] is taken on the
 // biased floats, so the low byte of each result is the code.  Statistics must be
 // finite.
+template <bool kBf16>
 __device__ __forceinline__ void fast_pair(uint32_t hx, float2 r, float2 mz, float2 top, uint32_t& mask, uint32_t b0,
                                           uint32_t b1, uint32_t& c0, uint32_t& c1) {
-  const float2 x = __half22float2(u2h2(hx));
+  const float2 x = Half16<kBf16>::to_f2(hx);
   const float f0 = __fmaf_rn(x.x, r.x, mz.x), f1 = __fmaf_rn(x.y, r.y, mz.y);
   const float e0 = __fmaf_rn(x.x, r.x, mz.x - f0), e1 = __fmaf_rn(x.y, r.y, mz.y - f1);   // x r - rint(x r)
   if (fabsf(e0) > kNearHalf) mask |= b0;
@@ -301,11 +307,12 @@ __device__ __forceinline__ void fast_pair(uint32_t hx, float2 r, float2 mz, floa
 // Exact codes of the flagged elements of one 8-element row (bit j of `flags` =
 // element j; element j's fp16 value at src[j * stride]); patches the 2-bit fields
 // of lo (bits 0-1 of each code) and hi (bits 2-3).  Rare: kept out of line.
+template <bool kBf16>
 __device__ __noinline__ uint2 patch_row(uint32_t flags, const uint16_t* src, int64_t stride, float scale, float zp,
                                         float maxq, uint32_t lo, uint32_t hi) {
   for (int j = 0; j < 8; ++j) {
     if (!((flags >> j) & 1u)) continue;
-    const uint32_t code = quant_code(h2f(src[j * stride]), scale, zp, maxq);
+    const uint32_t code = quant_code(Half16<kBf16>::to_f(src[j * stride]), scale, zp, maxq);
     lo = (lo & ~(3u << (2 * j))) | ((code & 3u) << (2 * j));
     hi = (hi & ~(3u << (2 * j))) | (((code >> 2) & 3u) << (2 * j));
   }
@@ -331,8 +338,10 @@ __device__ __forceinline__ int low_swz(int c, int byte) {
   return c * 32 + ((((byte >> 2) ^ (c >> 3)) & 7) << 2) + (byte & 3);
 }
 
+template <bool kBf16, bool kMetaBf16>
 __global__ void __launch_bounds__(kFastThreads, 4)
 quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
+  using T = Half16<kBf16>;
   constexpr int D = 128, G = 128, G4 = 32;
   __shared__ __align__(16) uint32_t s_red[8][64][2];   // per warp, per channel pair: (min, max) half2
   __shared__ float s_scale[D], s_zp[D], s_maxq[D], s_r[D];
@@ -355,46 +364,47 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
   if (tid == 0) s_nonfinite = 0;
 
   // per channel-pair min / max over this thread's 8 tokens
-  __half2 mn[4], mx[4];
+  uint32_t mn[4], mx[4];
 #pragma unroll
-  for (int w = 0; w < 4; ++w) mn[w] = mx[w] = u2h2(word_of(t.row[0], w));
+  for (int w = 0; w < 4; ++w) mn[w] = mx[w] = word_of(t.row[0], w);
 #pragma unroll
   for (int i = 1; i < 8; ++i)
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      const __half2 v = u2h2(word_of(t.row[i], w));
-      mn[w] = __hmin2_nan(mn[w], v);
-      mx[w] = __hmax2_nan(mx[w], v);
+      const uint32_t v = word_of(t.row[i], w);
+      mn[w] = T::min2(mn[w], v);
+      mx[w] = T::max2(mx[w], v);
     }
   // lanes l and l^16 hold the other token group of the same channels
 #pragma unroll
   for (int w = 0; w < 4; ++w) {
-    mn[w] = __hmin2_nan(mn[w], u2h2(__shfl_xor_sync(0xffffffffu, h22u(mn[w]), 16)));
-    mx[w] = __hmax2_nan(mx[w], u2h2(__shfl_xor_sync(0xffffffffu, h22u(mx[w]), 16)));
+    mn[w] = T::min2(mn[w], __shfl_xor_sync(0xffffffffu, mn[w], 16));
+    mx[w] = T::max2(mx[w], __shfl_xor_sync(0xffffffffu, mx[w], 16));
   }
   if (lane < 16) {
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
-      s_red[warp][4 * cg + w][0] = h22u(mn[w]);
-      s_red[warp][4 * cg + w][1] = h22u(mx[w]);
+      s_red[warp][4 * cg + w][0] = mn[w];
+      s_red[warp][4 * cg + w][1] = mx[w];
     }
   }
   __syncthreads();
   if (tid < 64) {  // channel pair tid: channels 2*tid, 2*tid+1
-    __half2 a2 = u2h2(s_red[0][tid][0]), b2 = u2h2(s_red[0][tid][1]);
+    uint32_t a2 = s_red[0][tid][0], b2 = s_red[0][tid][1];
 #pragma unroll
     for (int w = 1; w < 8; ++w) {
-      a2 = __hmin2_nan(a2, u2h2(s_red[w][tid][0]));
-      b2 = __hmax2_nan(b2, u2h2(s_red[w][tid][1]));
+      a2 = T::min2(a2, s_red[w][tid][0]);
+      b2 = T::max2(b2, s_red[w][tid][1]);
     }
+    const float2 mn2 = T::to_f2(a2), mx2 = T::to_f2(b2);
     uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.key_scale) + page * a.meta_s_page + h * a.meta_s_head;
     uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.key_zero) + page * a.meta_s_page + h * a.meta_s_head;
     bool nonfinite = false;
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       const int c = 2 * tid + e;
-      const float mnf = e ? __high2float(a2) : __low2float(a2);
-      const float mxf = e ? __high2float(b2) : __low2float(b2);
+      const float mnf = e ? mn2.y : mn2.x;
+      const float mxf = e ? mx2.y : mx2.x;
       const int r = bidx[c];
       const bool boosted = r < a.sentinel;
       const float maxq = boosted ? 15.0f : 3.0f;
@@ -404,8 +414,8 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
       s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq; s_r[c] = __frcp_rn(scale);
       s_row[c] = (boosted && r < K) ? r : -1;
       nonfinite |= !(isfinite(mnf) && isfinite(mxf) && isfinite(scale));
-      out_scale[c] = f2h(scale);
-      out_zero[c] = f2h(zp);
+      out_scale[c] = Half16<kMetaBf16>::meta(scale);
+      out_zero[c] = Half16<kMetaBf16>::meta(zp);
     }
     if (nonfinite) s_nonfinite = 1;
   }
@@ -434,18 +444,18 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
       const int kb = 8 * ((2 * w) & 3);
 #pragma unroll
       for (int i = 0; i < 8; ++i)
-        fast_pair(word_of(t.row[i], w), r, mz, top, m, 1u << (kb + i), 1u << (kb + 8 + i), ca[i], cb[i]);
+        fast_pair<kBf16>(word_of(t.row[i], w), r, mz, top, m, 1u << (kb + i), 1u << (kb + 8 + i), ca[i], cb[i]);
       uint32_t lo_a = pack4(ca[0], ca[1], ca[2], ca[3], 0) | (pack4(ca[4], ca[5], ca[6], ca[7], 0) << 8);
       uint32_t hi_a = pack4(ca[0], ca[1], ca[2], ca[3], 2) | (pack4(ca[4], ca[5], ca[6], ca[7], 2) << 8);
       uint32_t lo_b = pack4(cb[0], cb[1], cb[2], cb[3], 0) | (pack4(cb[4], cb[5], cb[6], cb[7], 0) << 8);
       uint32_t hi_b = pack4(cb[0], cb[1], cb[2], cb[3], 2) | (pack4(cb[4], cb[5], cb[6], cb[7], 2) << 8);
       const uint32_t fa = (m >> kb) & 0xffu, fb = (m >> (kb + 8)) & 0xffu;
       if (fa) {
-        const uint2 p = patch_row(fa, my_src + 2 * w, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], lo_a, hi_a);
+        const uint2 p = patch_row<kBf16>(fa, my_src + 2 * w, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], lo_a, hi_a);
         lo_a = p.x; hi_a = p.y;
       }
       if (fb) {
-        const uint2 p = patch_row(fb, my_src + 2 * w + 1, a.key_s_tok, s_scale[c + 1], s_zp[c + 1], s_maxq[c + 1], lo_b,
+        const uint2 p = patch_row<kBf16>(fb, my_src + 2 * w + 1, a.key_s_tok, s_scale[c + 1], s_zp[c + 1], s_maxq[c + 1], lo_b,
                                   hi_b);
         lo_b = p.x; hi_b = p.y;
       }
@@ -456,7 +466,7 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
 #pragma unroll 1
     for (int k = 0; k < 8; ++k) {
       const int c = 8 * cg + k;
-      const uint2 p = patch_row(0xffu, my_src + k, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], 0u, 0u);
+      const uint2 p = patch_row<kBf16>(0xffu, my_src + k, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], 0u, 0u);
       store(c, p.x, p.y);
     }
   }
@@ -475,8 +485,10 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
     reinterpret_cast<uint4*>(out_high)[i] = reinterpret_cast<const uint4*>(s_high)[i];
 }
 
+template <bool kBf16, bool kMetaBf16>
 __global__ void __launch_bounds__(kFastThreads, 4)
 quantize_value_d128_kernel(const KittyValueQuantArgs a) {
+  using T = Half16<kBf16>;
   constexpr int D4 = 32;
   __shared__ __align__(16) uint8_t s_codes[128 * D4];
   const int job = blockIdx.x / a.num_heads;
@@ -498,15 +510,16 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
   bool finite = true;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
-    __half2 lo = __hmin2_nan(u2h2(t.row[i].x), u2h2(t.row[i].y));
-    __half2 hi = __hmax2_nan(u2h2(t.row[i].x), u2h2(t.row[i].y));
-    lo = __hmin2_nan(lo, __hmin2_nan(u2h2(t.row[i].z), u2h2(t.row[i].w)));
-    hi = __hmax2_nan(hi, __hmax2_nan(u2h2(t.row[i].z), u2h2(t.row[i].w)));
-    __half2 mm = __halves2half2(__hmin_nan(__low2half(lo), __high2half(lo)),
-                                __hneg(__hmax_nan(__low2half(hi), __high2half(hi))));
+    uint32_t lo = T::min2(T::min2(t.row[i].x, t.row[i].y), T::min2(t.row[i].z, t.row[i].w));
+    uint32_t hi = T::max2(T::max2(t.row[i].x, t.row[i].y), T::max2(t.row[i].z, t.row[i].w));
+    lo = T::min2(lo, __funnelshift_l(lo, lo, 16));   // both halves: min of the pair
+    hi = T::max2(hi, __funnelshift_l(hi, hi, 16));
+    // (min, -max) in one pair: the sign flip of the high half negates it (NaN stays NaN)
+    uint32_t mm = (lo & 0x0000ffffu) | ((hi ^ 0x80000000u) & 0xffff0000u);
 #pragma unroll
-    for (int o = 1; o < 16; o <<= 1) mm = __hmin2_nan(mm, u2h2(__shfl_xor_sync(0xffffffffu, h22u(mm), o)));
-    const float mn = __low2float(mm), mx = -__high2float(mm);
+    for (int o = 1; o < 16; o <<= 1) mm = T::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    const float2 mmf = T::to_f2(mm);
+    const float mn = mmf.x, mx = -mmf.y;
     finite = finite && isfinite(mn) && isfinite(mx);
     mn_m = (mine == i) ? mn : mn_m;
     mx_m = (mine == i) ? mx : mx_m;
@@ -515,8 +528,8 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
   const float zp_m = tmin(tmax(rintf(__fdiv_rn(-mn_m, scale_m)), 0.0f), 3.0f);
   const float rcp_m = __frcp_rn(scale_m);
   if (cg < 8) {
-    out_scale[(8 * tg + cg) * a.meta_s_tok] = f2h(scale_m);
-    out_zero[(8 * tg + cg) * a.meta_s_tok] = f2h(zp_m);
+    out_scale[(8 * tg + cg) * a.meta_s_tok] = Half16<kMetaBf16>::meta(scale_m);
+    out_zero[(8 * tg + cg) * a.meta_s_tok] = Half16<kMetaBf16>::meta(zp_m);
   }
   finite = __all_sync(0xffffffffu, finite);   // warp-uniform: the shuffles below run in every lane
   const int base_lane = threadIdx.x & 16;
@@ -536,13 +549,13 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
       uint32_t c[8];
 #pragma unroll
       for (int w = 0; w < 4; ++w)
-        fast_pair(word_of(t.row[i], w), r2, mz, top, m, 1u << (ib + 2 * w), 1u << (ib + 2 * w + 1), c[2 * w],
+        fast_pair<kBf16>(word_of(t.row[i], w), r2, mz, top, m, 1u << (ib + 2 * w), 1u << (ib + 2 * w + 1), c[2 * w],
                   c[2 * w + 1]);
       bits[i] = pack4(c[0], c[1], c[2], c[3], 0) | (pack4(c[4], c[5], c[6], c[7], 0) << 8);
       const uint32_t f = (m >> ib) & 0xffu;
       const float scale = __shfl_sync(0xffffffffu, scale_m, base_lane + i);
       if (f && 8 * tg + i < n_valid)
-        bits[i] = patch_row(f, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, bits[i], 0u).x;
+        bits[i] = patch_row<kBf16>(f, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, bits[i], 0u).x;
     }
   } else {   // non-finite statistics in this warp: the exact path (rows beyond n_valid read as zeros)
 #pragma unroll
@@ -551,7 +564,7 @@ quantize_value_d128_kernel(const KittyValueQuantArgs a) {
       const float zp = __shfl_sync(0xffffffffu, zp_m, base_lane + i);
       uint32_t b;
       if (8 * tg + i < n_valid) {
-        b = patch_row(0xffu, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, 0u, 0u).x;
+        b = patch_row<kBf16>(0xffu, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, 0u, 0u).x;
       } else {
         b = (quant_code(0.0f, scale, zp, 3.0f) & 3u) * 0x5555u;
       }
@@ -592,6 +605,9 @@ int quantize_key_pages_impl(const KittyKeyQuantArgs* a, void* stream) {
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_key_pages: head_dim and group must be multiples of 4");
   if (a->d_boost < 0 || a->d_boost > 255 || a->sentinel < 0)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_key_pages: d_boost must be in [0,255], sentinel >= 0");
+  if (a->dtype != KITTY_DTYPE_F16 && a->dtype != KITTY_DTYPE_BF16 && a->dtype != KITTY_DTYPE_BF16_F16META)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_key_pages: unknown dtype");
+  const int dt = a->dtype;
   if (!a->key || !a->key_off || !a->boost_idx || !a->dst_page || !a->key_low || !a->key_scale || !a->key_zero ||
       (a->d_boost > 0 && !a->key_high))
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_key_pages: NULL pointer");
@@ -606,13 +622,17 @@ int quantize_key_pages_impl(const KittyKeyQuantArgs* a, void* stream) {
       fast_source_ok(a->key, a->key_s_tok, a->key_s_ch) && (a->key_s_head % 8) == 0 &&
       aligned(a->key_low, 16) && (a->low_s_page % 16) == 0 && (a->low_s_head % 16) == 0 &&
       (a->d_boost == 0 || (aligned(a->key_high, 16) && (a->high_s_page % 16) == 0 && (a->high_s_head % 16) == 0))) {
-    quantize_key_d128_kernel<<<a->n_jobs * a->num_heads, kFastThreads, 0, as_stream(stream)>>>(*a);
+    auto fast = dt == KITTY_DTYPE_BF16 ? quantize_key_d128_kernel<true, true>
+                : dt == KITTY_DTYPE_BF16_F16META ? quantize_key_d128_kernel<true, false>
+                                                 : quantize_key_d128_kernel<false, false>;
+    fast<<<a->n_jobs * a->num_heads, kFastThreads, 0, as_stream(stream)>>>(*a);
     return check_launch("quantize_key_d128_kernel");
   }
-  if (smem > 48 * 1024) {
-    cudaFuncSetAttribute(quantize_key_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  }
-  quantize_key_kernel<<<a->n_jobs * a->num_heads, kQuantThreads, smem, as_stream(stream)>>>(*a);
+  auto kern = dt == KITTY_DTYPE_BF16 ? quantize_key_kernel<true, true>
+              : dt == KITTY_DTYPE_BF16_F16META ? quantize_key_kernel<true, false>
+                                               : quantize_key_kernel<false, false>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  kern<<<a->n_jobs * a->num_heads, kQuantThreads, smem, as_stream(stream)>>>(*a);
   return check_launch("quantize_key_kernel");
 }
 
@@ -625,6 +645,9 @@ int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream) {
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_value_pages: head_dim and group must be multiples of 4");
   if (!a->value || !a->value_off || !a->dst_page || !a->val_codes || !a->val_scale || !a->val_zero)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_value_pages: NULL pointer");
+  if (a->dtype != KITTY_DTYPE_F16 && a->dtype != KITTY_DTYPE_BF16 && a->dtype != KITTY_DTYPE_BF16_F16META)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "quantize_value_pages: unknown dtype");
+  const int dt = a->dtype;
   const size_t smem = value_smem_bytes(a->head_dim, a->group);
   if (smem > 200 * 1024)
     return fail(KITTY_ERR_UNSUPPORTED, "quantize_value_pages: head_dim*group too large for one CTA");
@@ -633,13 +656,17 @@ int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream) {
   if (a->head_dim == 128 && a->group == 128 && fast_source_ok(a->value, a->val_s_tok, a->val_s_ch) &&
       (a->val_s_head % 8) == 0 && aligned(a->val_codes, 16) && (a->codes_s_page % 16) == 0 &&
       (a->codes_s_head % 16) == 0) {
-    quantize_value_d128_kernel<<<a->n_jobs * a->num_heads, kFastThreads, 0, as_stream(stream)>>>(*a);
+    auto fast = dt == KITTY_DTYPE_BF16 ? quantize_value_d128_kernel<true, true>
+                : dt == KITTY_DTYPE_BF16_F16META ? quantize_value_d128_kernel<true, false>
+                                                 : quantize_value_d128_kernel<false, false>;
+    fast<<<a->n_jobs * a->num_heads, kFastThreads, 0, as_stream(stream)>>>(*a);
     return check_launch("quantize_value_d128_kernel");
   }
-  if (smem > 48 * 1024) {
-    cudaFuncSetAttribute(quantize_value_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
-  }
-  quantize_value_kernel<<<a->n_jobs * a->num_heads, kQuantThreads, smem, as_stream(stream)>>>(*a);
+  auto kern = dt == KITTY_DTYPE_BF16 ? quantize_value_kernel<true, true>
+              : dt == KITTY_DTYPE_BF16_F16META ? quantize_value_kernel<true, false>
+                                               : quantize_value_kernel<false, false>;
+  if (smem > 48 * 1024) cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  kern<<<a->n_jobs * a->num_heads, kQuantThreads, smem, as_stream(stream)>>>(*a);
   return check_launch("quantize_value_kernel");
 }
 
@@ -651,7 +678,10 @@ int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream) {
   if (!a->key_low || !a->key_scale || !a->key_zero || !a->src_page || !a->head || !a->boost_idx || !a->out ||
       !a->out_off || (a->d_boost > 0 && !a->key_high))
     return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_key_pages: NULL pointer");
-  dequantize_key_kernel<<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
+  if (a->dtype != KITTY_DTYPE_F16 && a->dtype != KITTY_DTYPE_BF16)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_key_pages: dtype must be KITTY_DTYPE_F16 or KITTY_DTYPE_BF16");
+  if (a->dtype == KITTY_DTYPE_BF16) dequantize_key_kernel<true><<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
+  else dequantize_key_kernel<false><<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
   return check_launch("dequantize_key_kernel");
 }
 

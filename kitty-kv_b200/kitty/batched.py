@@ -5,8 +5,9 @@ A decode step appends one token to each of n sequences with ONE library call
 capturable) and attends over them with one more (``kitty_paged_decode`` with a
 sequence map).  Per sequence it runs the state machine of the reference's
 ``KittyInferencePipeline.push_token`` (``kitty/pipeline.py:115-181``): the first
-``sink_size`` tokens stay in fp16 sinks, later tokens fill a G-token fp16 buffer,
-and a full buffer is quantised into a freshly allocated page.  The values of a
+``sink_size`` tokens stay unquantised (float16 or bfloat16, ``config.dtype``) in the
+sinks, later tokens fill a G-token buffer, and a full buffer is quantised into a
+freshly allocated page.  The values of a
 page are those of the same G tokens (the pipeline's ``align_values=True``
 mode), so decode pairs every key with its own value.  Pages come from a
 device-side free stack shared by all layers; it replaces the host free mask of
@@ -28,6 +29,7 @@ import torch
 from .config import KittyConfig
 from .kernels import _lib
 from .kernels.attention import paged_attention_batched
+from .layout import torch_dtype
 
 
 class BatchedKVCache:
@@ -41,8 +43,6 @@ class BatchedKVCache:
     def __init__(self, config: KittyConfig, boost_idx_uint8: torch.Tensor, max_seqs: int,
                  num_pages: Optional[int] = None, max_pages_per_seq: Optional[int] = None,
                  device: Optional[torch.device] = None) -> None:
-        if config.dtype != "float16":
-            raise RuntimeError("BatchedKVCache stores float16 buffers and pools (bfloat16 is not supported yet)")
         self.config = config
         dev = torch.device(device if device is not None else config.device)
         if dev.type != "cuda":
@@ -63,7 +63,8 @@ class BatchedKVCache:
         if tuple(bidx.shape) != (L, H, D):
             raise RuntimeError(f"boost_idx must be ({L}, {H}, {D}) or ({H}, {D}) uint8")
         self.boost_idx = bidx.contiguous()
-        f16, i32 = torch.float16, torch.int32
+        f16, i32 = torch_dtype(config.dtype), torch.int32      # float16 or bfloat16 buffers / metadata
+        self.dtype = f16
         P, B, M = self.num_pages, self.max_seqs, self.max_pages_per_seq
         # pools (the layout manager's shapes, kitty/layout.py:128-147)
         self.key_baseline = torch.zeros(P, H, D, G // 4, dtype=torch.uint8, device=dev)
@@ -110,6 +111,7 @@ class BatchedKVCache:
         st.val_codes, st.val_meta = self.value_pool.data_ptr(), self.value_metadata.data_ptr()
         st.job_off, st.job_page = self._job_off[l].data_ptr(), self._job_page[l].data_ptr()
         st.job_slot = self._job_slot[l].data_ptr()
+        st.dtype = _lib.dtype_code(self.dtype)
         return st
 
     def state(self, layer_id: int) -> _lib.CacheState:
@@ -137,14 +139,14 @@ class BatchedKVCache:
             _lib.check(lib.kitty_cache_reset(st, self._stream()), "kitty_cache_reset")
 
     def append(self, layer_id: int, seq_ids, key: torch.Tensor, value: torch.Tensor) -> None:
-        """Append token row i of key / value ((n, H, D) float16) to slot seq_ids[i] of
+        """Append token row i of key / value ((n, H, D), the cache's dtype) to slot seq_ids[i] of
         ``layer_id``; slots whose buffer fills are quantised into new pages."""
         ids = self._ids(seq_ids)
         n = ids.numel()
         H, D = self.config.num_kv_heads, self.config.head_dim
         for t, name in ((key, "key"), (value, "value")):
-            if t.dtype != torch.float16 or t.device != self.device or tuple(t.shape) != (n, H, D):
-                raise RuntimeError(f"{name} must be ({n}, {H}, {D}) float16 on {self.device}")
+            if t.dtype != self.dtype or t.device != self.device or tuple(t.shape) != (n, H, D):
+                raise RuntimeError(f"{name} must be ({n}, {H}, {D}) {self.dtype} on {self.device}")
         if key.stride(2) != 1:
             key = key.contiguous()
         if value.stride(2) != 1:
@@ -157,7 +159,7 @@ class BatchedKVCache:
     def prefill(self, layer_id: int, seq_ids, key: torch.Tensor, value: torch.Tensor, lengths) -> None:
         """Append lengths[i] tokens to slot seq_ids[i] of ``layer_id`` in one call: the
         tokens of the i-th sequence are the next lengths[i] rows of key / value
-        ((sum(lengths), H, D) float16, sequences one after another).  Same result as
+        ((sum(lengths), H, D), the cache's dtype, sequences one after another).  Same result as
         appending them one at a time; full groups of G tokens are quantised straight
         from ``key`` / ``value``.  ``lengths``: host integers (they size the launch)."""
         lens = [int(x) for x in (lengths.tolist() if isinstance(lengths, torch.Tensor) else lengths)]
@@ -168,8 +170,8 @@ class BatchedKVCache:
         H, D, G = self.config.num_kv_heads, self.config.head_dim, self.config.q_buffer_size
         N = sum(lens)
         for t, name in ((key, "key"), (value, "value")):
-            if t.dtype != torch.float16 or t.device != self.device or tuple(t.shape) != (N, H, D):
-                raise RuntimeError(f"{name} must be ({N}, {H}, {D}) float16 on {self.device}")
+            if t.dtype != self.dtype or t.device != self.device or tuple(t.shape) != (N, H, D):
+                raise RuntimeError(f"{name} must be ({N}, {H}, {D}) {self.dtype} on {self.device}")
         if key.stride(2) != 1 or key.stride() != value.stride():
             key, value = key.contiguous(), value.contiguous()
         starts = [0] * n
@@ -201,7 +203,7 @@ class BatchedKVCache:
 
     def decode(self, layer_id: int, q: torch.Tensor, seq_ids, out: Optional[torch.Tensor] = None,
                sm_scale: Optional[float] = None, num_splits: int = 0) -> torch.Tensor:
-        """Decode attention of row i of q ((n, Hq, D) float16) over slot seq_ids[i]."""
+        """Decode attention of row i of q ((n, Hq, D)) over slot seq_ids[i]; float16 output."""
         ids = self._ids(seq_ids)
         l = layer_id
         return paged_attention_batched(

@@ -23,8 +23,8 @@ class KittyConfig:
     local_value_window (R): most recent values kept in fp16.
     boost_rate: fraction of key channels stored at INT4 (0.125 Kitty, 0.25 Kitty-Pro).
     max_seq_len / max_batch_size: sizing of the page pool.
-    dtype: fp16 buffer / metadata type ("float16"; "bfloat16" is accepted by the
-    config but the B200 kernels currently require float16).
+    dtype: buffer / metadata type, "float16" or "bfloat16" (the B200 kernels take
+    both; decode outputs are float16 either way, as in the reference).
     device: CUDA device of the pools and buffers.
     """
 

@@ -16,13 +16,14 @@ from typing import Dict, Optional, Tuple
 
 import torch
 
-ABI_VERSION = 2
+ABI_VERSION = 3
 LIB_NAME = "libkitty_b200.so"
 _LIB_PATH = Path(os.environ.get("KITTY_B200_LIB", Path(__file__).resolve().parent.parent / LIB_NAME))
 
 c_i32, c_i64, c_ptr, c_f32, c_size = ctypes.c_int32, ctypes.c_int64, ctypes.c_void_p, ctypes.c_float, ctypes.c_size_t
 
 KITTY_OK = 0
+DTYPE_F16, DTYPE_BF16 = 0, 1
 ERROR_NAMES = {1: "invalid argument", 2: "unsupported", 3: "CUDA error", 4: "workspace"}
 
 
@@ -32,7 +33,7 @@ class KeyQuantArgs(ctypes.Structure):
                 ("key_low", c_ptr), ("key_high", c_ptr), ("key_scale", c_ptr), ("key_zero", c_ptr),
                 ("low_s_page", c_i64), ("low_s_head", c_i64), ("high_s_page", c_i64), ("high_s_head", c_i64),
                 ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("n_jobs", c_i32), ("num_heads", c_i32),
-                ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32), ("sentinel", c_i32)]
+                ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32), ("sentinel", c_i32), ("dtype", c_i32)]
 
 
 class ValueQuantArgs(ctypes.Structure):
@@ -40,7 +41,7 @@ class ValueQuantArgs(ctypes.Structure):
                 ("val_s_ch", c_i64), ("n_valid", c_ptr), ("dst_page", c_ptr), ("val_codes", c_ptr),
                 ("val_scale", c_ptr), ("val_zero", c_ptr), ("codes_s_page", c_i64), ("codes_s_head", c_i64),
                 ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("meta_s_tok", c_i64), ("n_jobs", c_i32),
-                ("num_heads", c_i32), ("head_dim", c_i32), ("group", c_i32)]
+                ("num_heads", c_i32), ("head_dim", c_i32), ("group", c_i32), ("dtype", c_i32)]
 
 
 class KeyDequantArgs(ctypes.Structure):
@@ -49,7 +50,7 @@ class KeyDequantArgs(ctypes.Structure):
                 ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("src_page", c_ptr), ("head", c_ptr),
                 ("boost_idx", c_ptr), ("bidx_s_head", c_i64), ("out", c_ptr), ("out_off", c_ptr),
                 ("out_s_ch", c_i64), ("out_s_tok", c_i64), ("n_jobs", c_i32), ("num_heads", c_i32),
-                ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32)]
+                ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32), ("dtype", c_i32)]
 
 
 class DecodeArgs(ctypes.Structure):
@@ -67,7 +68,7 @@ class DecodeArgs(ctypes.Structure):
                 ("tail_v", c_ptr), ("tv_s_seq", c_i64), ("tv_s_head", c_i64), ("tv_s_tok", c_i64),
                 ("tail_len", c_ptr), ("tail_len_all", c_i32),
                 ("max_pages_per_seq", c_i32), ("num_splits", c_i32),
-                ("workspace", c_ptr), ("workspace_bytes", c_size), ("seq_map", c_ptr)]
+                ("workspace", c_ptr), ("workspace_bytes", c_size), ("seq_map", c_ptr), ("dtype", c_i32)]
 
 
 class CacheState(ctypes.Structure):
@@ -78,7 +79,7 @@ class CacheState(ctypes.Structure):
                 ("sink_len", c_ptr), ("tail_len", c_ptr), ("num_pages", c_ptr), ("claim", c_ptr),
                 ("block_table", c_ptr), ("free_pages", c_ptr), ("free_top", c_ptr),
                 ("key_low", c_ptr), ("key_high", c_ptr), ("key_meta", c_ptr), ("val_codes", c_ptr),
-                ("val_meta", c_ptr), ("job_off", c_ptr), ("job_page", c_ptr), ("job_slot", c_ptr)]
+                ("val_meta", c_ptr), ("job_off", c_ptr), ("job_page", c_ptr), ("job_slot", c_ptr), ("dtype", c_i32)]
 
 
 class PrefillArgs(ctypes.Structure):
@@ -172,6 +173,29 @@ def force_decode_variant(name: str) -> str:
     prev = ctypes.c_int(-1)
     check(load().kitty_decode_force_variant(DECODE_VARIANTS[name], ctypes.byref(prev)), "kitty_decode_force_variant")
     return {v: k for k, v in DECODE_VARIANTS.items()}[prev.value]
+
+
+def dtype_code(dtype: torch.dtype) -> int:
+    """KITTY_DTYPE_* of a 16-bit float torch dtype; other dtypes raise."""
+    if dtype == torch.float16:
+        return DTYPE_F16
+    if dtype == torch.bfloat16:
+        return DTYPE_BF16
+    raise RuntimeError(f"expected a float16 or bfloat16 tensor, got {dtype}")
+
+
+DTYPE_BF16_F16META = 3
+
+
+def quant_dtype_code(src: torch.dtype, meta: torch.dtype) -> int:
+    """KITTY_DTYPE_* of a quantiser call: the source's type, metadata of the same
+    type, or fp16 metadata for a bf16 source (the reference's functional forms)."""
+    code = dtype_code(src)
+    if meta == src:
+        return code
+    if src == torch.bfloat16 and meta == torch.float16:
+        return DTYPE_BF16_F16META
+    raise RuntimeError(f"metadata dtype {meta} does not go with a {src} source")
 
 
 def require_cuda(*tensors: Optional[torch.Tensor]) -> torch.device:

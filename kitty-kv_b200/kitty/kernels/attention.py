@@ -13,7 +13,8 @@ Drop-in for ``kitty/kernels/attention.py`` of the reference:
 Semantics (``attention.py:136-189``): for query head qh and KV head
 h = qh // (Hq/H), keys are [sinks ; pages in block-table order ; key tail] and
 values [sinks ; value pages ; value tail]; out = softmax(q.k / sqrt(D)) . v,
-accumulated in float32 and returned as float16.
+accumulated in float32 and returned as float16 (also for a bfloat16 cache, as the
+reference's ``.to(torch.float16)`` at ``attention.py:189`` does).
 """
 
 from __future__ import annotations
@@ -98,8 +99,9 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
                  (value_pool, "value_pool"), (value_meta, "value_meta")):
         if not t.is_contiguous():
             raise RuntimeError(f"{n} must be contiguous")
-    if key_meta.dtype != torch.float16 or value_meta.dtype != torch.float16:
-        raise RuntimeError("metadata pools must be float16; bfloat16 pools are not supported yet")
+    if key_meta.dtype != value_meta.dtype or key_meta.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("metadata pools must both be float16 or both bfloat16")
+    h16 = key_meta.dtype      # the cache's 16-bit type: q, sinks and tails are read in it
     if tuple(value_pool.shape) != (P, H, G, D // 4) or tuple(key_meta.shape) != (P, H, 2, D):
         raise RuntimeError("pool shapes are inconsistent")
     if boost_idx.dtype != torch.uint8 or tuple(boost_idx.shape) != (H, D) or boost_idx.stride(1) != 1:
@@ -117,13 +119,13 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
         raise RuntimeError("block_table rows need unit stride")
     if num_pages.dtype != torch.int32 or num_pages.numel() != rows:
         raise RuntimeError("num_pages must be (B,) int32 (one entry per cache slot with seq_map)")
-    if q.dtype != torch.float16:
-        q = q.to(torch.float16)
+    if q.dtype != h16:
+        q = q.to(h16)
     if q.stride(-1) != 1:
         q = q.contiguous()
     for t, n in ((sink_k, "sink_k"), (sink_v, "sink_v"), (tail_k, "tail_k"), (tail_v, "tail_v")):
-        if t is not None and (t.dtype != torch.float16 or t.dim() != 4 or t.shape[1] != H or t.shape[3] != D):
-            raise RuntimeError(f"{n} must be (B, H, T, D) float16")
+        if t is not None and (t.dtype != h16 or t.dim() != 4 or t.shape[1] != H or t.shape[3] != D):
+            raise RuntimeError(f"{n} must be (B, H, T, D) {h16} (the metadata pools' dtype)")
     sink_t, sink_all = _as_len(sink_len, "sink_len", rows, dev)
     tail_t, tail_all = _as_len(tail_len, "tail_len", rows, dev)
     if sink_t is None and sink_all > 0 and (sink_k is None or sink_all > min(sink_k.shape[2], sink_v.shape[2])):
@@ -154,6 +156,7 @@ def paged_attention_batched(q: torch.Tensor, block_table: torch.Tensor, num_page
     a.tail_len, a.tail_len_all = _lib.ptr(tail_t), tail_all
     a.max_pages_per_seq, a.num_splits = maxp, int(num_splits)
     a.seq_map = _lib.ptr(seq_map)
+    a.dtype = _lib.dtype_code(h16)
     lib = _lib.load()
     nbytes = _lib.c_size(0)
     _lib.check(lib.kitty_paged_decode_workspace_size(a, nbytes, None), "kitty_paged_decode_workspace_size")

@@ -20,8 +20,8 @@ def _launch(tensor_2bits, tensor_high_2bits, scale, zero_point, boost_idx, D_boo
     for t, n in ((tensor_2bits, "tensor_2bits"), (tensor_high_2bits, "tensor_high_2bits")):
         if not t.is_contiguous():
             raise RuntimeError(f"{n} must be contiguous")
-    if scale.dtype != torch.float16 or zero_point.dtype != torch.float16 or out.dtype != torch.float16:
-        raise RuntimeError("scale, zero_point and out must be float16")
+    if not (scale.dtype == zero_point.dtype == out.dtype) or out.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("scale, zero_point and out must all be float16 or all bfloat16")
     if scale.stride(0) != 1 or zero_point.stride(0) != 1 or boost_idx.stride(0) != 1:
         raise RuntimeError("scale, zero_point and boost_idx need unit stride")
     a = _lib.KeyDequantArgs()
@@ -34,6 +34,7 @@ def _launch(tensor_2bits, tensor_high_2bits, scale, zero_point, boost_idx, D_boo
     a.out = out.data_ptr(); a.out_off = _lib.zeros_const(dev, torch.int64).data_ptr()
     a.out_s_ch, a.out_s_tok = out.stride(0), out.stride(1)
     a.n_jobs, a.num_heads, a.head_dim, a.group, a.d_boost = 1, 1, D, G4 * 4, int(D_boost)
+    a.dtype = _lib.dtype_code(out.dtype)
     lib = _lib.load()
     _lib.check(lib.kitty_dequantize_key_pages(a, _lib.stream_ptr(dev)), "kitty_dequantize_key_pages")
 
@@ -41,8 +42,8 @@ def _launch(tensor_2bits, tensor_high_2bits, scale, zero_point, boost_idx, D_boo
 def dequantize_key_page(tensor_2bits: torch.Tensor, tensor_high_2bits: torch.Tensor, scale: torch.Tensor,
                         zero_point: torch.Tensor, boost_idx: torch.Tensor, D_boost: int,
                         out: torch.Tensor) -> None:
-    """Dequantise one key page into a pre-allocated (D, G) float16 tensor
-    (reference signature ``dequantize_key.py:169-177``)."""
+    """Dequantise one key page into a pre-allocated (D, G) float16 (or, with bfloat16
+    metadata, bfloat16) tensor (reference signature ``dequantize_key.py:169-177``)."""
     D, G4 = tensor_2bits.shape
     if tuple(out.shape) != (D, G4 * 4):
         raise RuntimeError(f"out must be ({D}, {G4 * 4})")

@@ -25,9 +25,11 @@ import torch
 from . import _lib
 
 
-def _check_fp16(t: torch.Tensor, name: str) -> None:
-    if t.dtype != torch.float16:
-        raise RuntimeError(f"{name} must be float16 (got {t.dtype}); bfloat16 pools are not supported yet")
+def _check_h16(t: torch.Tensor, name: str) -> int:
+    """KITTY_DTYPE_* of a float16 / bfloat16 tensor (other dtypes raise)."""
+    if t.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError(f"{name} must be float16 or bfloat16 (got {t.dtype})")
+    return _lib.dtype_code(t.dtype)
 
 
 def quantize_key_pages(key_src: torch.Tensor, src_offsets: torch.Tensor, src_strides: Tuple[int, int, int],
@@ -43,8 +45,9 @@ def quantize_key_pages(key_src: torch.Tensor, src_offsets: torch.Tensor, src_str
     ``key_high (P,H,K,G/4)``, ``key_meta (P,H,2,D)``.
     """
     dev = _lib.require_cuda(key_src, src_offsets, boost_idx, dst_pages, key_low, key_high, key_meta)
-    _check_fp16(key_src, "key")
-    _check_fp16(key_meta, "key_meta")
+    _check_h16(key_src, "key")
+    _check_h16(key_meta, "key_meta")
+    code = _lib.quant_dtype_code(key_src.dtype, key_meta.dtype)
     if src_offsets.dtype != torch.int64 or dst_pages.dtype != torch.int32:
         raise RuntimeError("src_offsets must be int64 and dst_pages int32")
     if boost_idx.dtype != torch.uint8 or boost_idx.dim() != 2 or boost_idx.stride(1) != 1:
@@ -68,6 +71,7 @@ def quantize_key_pages(key_src: torch.Tensor, src_offsets: torch.Tensor, src_str
     a.meta_s_page, a.meta_s_head = key_meta.stride(0), key_meta.stride(1)
     a.n_jobs, a.num_heads, a.head_dim, a.group = n, num_heads, head_dim, group
     a.d_boost, a.sentinel = int(d_boost), int(sentinel)
+    a.dtype = code
     lib = _lib.load()
     _lib.check(lib.kitty_quantize_key_pages(a, _lib.stream_ptr(dev)), "kitty_quantize_key_pages")
 
@@ -86,6 +90,7 @@ def _launch_single(key: torch.Tensor, boost_idx: torch.Tensor, d_boost: int, sen
     a.key_scale = scale.data_ptr(); a.key_zero = zero.data_ptr()
     a.n_jobs, a.num_heads, a.head_dim, a.group = 1, 1, D, G
     a.d_boost, a.sentinel = int(d_boost), int(sentinel)
+    a.dtype = _lib.quant_dtype_code(key.dtype, scale.dtype)
     lib = _lib.load()
     _lib.check(lib.kitty_quantize_key_pages(a, _lib.stream_ptr(dev)), "kitty_quantize_key_pages")
 
@@ -96,7 +101,7 @@ def _validate_single(key, boost_idx, D_boost):
     D, G = key.shape
     if G % 4 != 0:
         raise AssertionError("G must be divisible by 4 for uint8 packing")
-    _check_fp16(key, "key")
+    _check_h16(key, "key")
     if boost_idx.shape != (D,) or boost_idx.dtype != torch.uint8:
         raise RuntimeError("boost_idx must be a (D,) uint8 tensor")
     if boost_idx.stride(0) != 1:
@@ -112,7 +117,7 @@ def quantize_key_page_torch(key: torch.Tensor, boost_idx: torch.Tensor, D_boost:
     dev = _lib.require_cuda(key, boost_idx)
     low = torch.empty(D, G // 4, dtype=torch.uint8, device=dev)
     high = torch.empty(D_boost, G // 4, dtype=torch.uint8, device=dev)
-    meta = torch.empty(2, D, dtype=torch.float16, device=dev)
+    meta = torch.empty(2, D, dtype=torch.float16, device=dev)   # the reference returns fp16
     _launch_single(key, boost_idx, D_boost, sentinel, low, high, meta[0], meta[1])
     return low, high, meta[0], meta[1]
 
@@ -133,8 +138,9 @@ def quantize_key_page(key: torch.Tensor, boost_idx: torch.Tensor, D_boost: int, 
     if out_scale.numel() != D or out_zero.numel() != D:
         raise RuntimeError("out_scale / out_zero must have D elements")
     direct = (out_baseline.is_contiguous() and out_boost.is_contiguous() and out_scale.is_contiguous()
-              and out_zero.is_contiguous() and out_scale.dtype == torch.float16
-              and out_zero.dtype == torch.float16)
+              and out_zero.is_contiguous() and out_scale.dtype == out_zero.dtype
+              and out_scale.dtype in (torch.float16, torch.bfloat16)
+              and (out_scale.dtype == key.dtype or out_scale.dtype == torch.float16))
     if direct:
         _launch_single(key, boost_idx, D_boost, sentinel, out_baseline, out_boost, out_scale, out_zero)
         return

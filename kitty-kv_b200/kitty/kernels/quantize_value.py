@@ -30,8 +30,7 @@ def quantize_value_pages(value_src: torch.Tensor, src_offsets: torch.Tensor, src
     ``n_valid[j]`` read as zero (the reference pads a partial buffer with zeros,
     ``kitty/pipeline.py:238-243``)."""
     dev = _lib.require_cuda(value_src, src_offsets, dst_pages, val_codes, val_meta, n_valid)
-    if value_src.dtype != torch.float16 or val_meta.dtype != torch.float16:
-        raise RuntimeError("value and value_meta must be float16; bfloat16 pools are not supported yet")
+    code = _lib.quant_dtype_code(value_src.dtype, val_meta.dtype)
     if src_offsets.dtype != torch.int64 or dst_pages.dtype != torch.int32:
         raise RuntimeError("src_offsets must be int64 and dst_pages int32")
     if n_valid is not None and (n_valid.dtype != torch.int32 or n_valid.numel() != dst_pages.numel()):
@@ -48,6 +47,7 @@ def quantize_value_pages(value_src: torch.Tensor, src_offsets: torch.Tensor, src
     a.codes_s_page, a.codes_s_head = val_codes.stride(0), val_codes.stride(1)
     a.meta_s_page, a.meta_s_head, a.meta_s_tok = val_meta.stride(0), val_meta.stride(1), val_meta.stride(2)
     a.n_jobs, a.num_heads, a.head_dim, a.group = dst_pages.numel(), num_heads, head_dim, group
+    a.dtype = code
     lib = _lib.load()
     _lib.check(lib.kitty_quantize_value_pages(a, _lib.stream_ptr(dev)), "kitty_quantize_value_pages")
 
@@ -62,6 +62,7 @@ def _launch_single(value: torch.Tensor, codes: torch.Tensor, scale: torch.Tensor
     a.val_codes = codes.data_ptr(); a.val_scale = scale.data_ptr(); a.val_zero = zero.data_ptr()
     a.meta_s_tok = scale.stride(0)
     a.n_jobs, a.num_heads, a.head_dim, a.group = 1, 1, D, G
+    a.dtype = _lib.quant_dtype_code(value.dtype, scale.dtype)
     lib = _lib.load()
     _lib.check(lib.kitty_quantize_value_pages(a, _lib.stream_ptr(dev)), "kitty_quantize_value_pages")
 
@@ -72,8 +73,8 @@ def _validate(value):
     G, D = value.shape
     if D % 4 != 0:
         raise AssertionError("head_dim D must be divisible by 4 for packing")
-    if value.dtype != torch.float16:
-        raise RuntimeError(f"value must be float16 (got {value.dtype})")
+    if value.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError(f"value must be float16 or bfloat16 (got {value.dtype})")
     return G, D
 
 
@@ -82,7 +83,7 @@ def quantize_value_page_torch(value: torch.Tensor) -> Tuple[torch.Tensor, torch.
     G, D = _validate(value)
     dev = _lib.require_cuda(value)
     codes = torch.empty(G, D // 4, dtype=torch.uint8, device=dev)
-    meta = torch.empty(2, G, dtype=torch.float16, device=dev)
+    meta = torch.empty(2, G, dtype=torch.float16, device=dev)   # the reference returns fp16
     _launch_single(value, codes, meta[0], meta[1])
     return codes, meta[0], meta[1]
 
@@ -95,8 +96,8 @@ def quantize_value_page(value: torch.Tensor, out_packed: torch.Tensor, out_scale
     if tuple(out_packed.shape) != (G, D // 4) or out_scale.numel() != G or out_zero.numel() != G:
         raise RuntimeError("out_packed must be (G, D/4); out_scale/out_zero must have G elements")
     same_stride = out_scale.dim() == 1 and out_zero.dim() == 1 and out_scale.stride(0) == out_zero.stride(0)
-    if (out_packed.is_contiguous() and same_stride and out_scale.dtype == torch.float16
-            and out_zero.dtype == torch.float16):
+    if (out_packed.is_contiguous() and same_stride and out_scale.dtype == out_zero.dtype
+            and (out_scale.dtype == value.dtype or out_scale.dtype == torch.float16)):
         _launch_single(value, out_packed, out_scale, out_zero)
         return
     codes, scale, zero = quantize_value_page_torch(value)

@@ -29,7 +29,12 @@ Float32 semantics reproduced from torch:
 * ``torch.round`` is round-half-to-even (``np.rint``);
 * division is IEEE float32 round-to-nearest;
 * ``torch.maximum/minimum`` propagate NaN (``np.maximum/minimum`` do too);
-* ``.to(float16)`` rounds to nearest even (``astype(np.float16)``).
+* ``.to(float16)`` rounds to nearest even (``astype(np.float16)``);
+* a bfloat16 cache (``dtype="bfloat16"``): inputs widen exactly (``.float()``),
+  and the fp16 scale / zero-point the quantisers return are copied into bf16
+  pool views (``kitty/kernels/quantize_key.py:261-269``), i.e. rounded to fp16
+  and then to bf16 (nearest even, ``bf16_round``).  bf16 arrays are passed and
+  returned here as float32 arrays holding bf16 values.
 """
 
 from __future__ import annotations
@@ -41,6 +46,34 @@ import numpy as np
 
 F32 = np.float32
 _EPS_RANGE = F32(1e-8)
+
+
+# ---------------------------------------------------------------------------
+# 16-bit float types
+# ---------------------------------------------------------------------------
+
+def bf16_round(x: np.ndarray) -> np.ndarray:
+    """float32 -> nearest bfloat16 (ties to even), returned as float32; NaN stays NaN."""
+    x = np.ascontiguousarray(np.asarray(x, dtype=F32))
+    b = x.view(np.uint32).astype(np.uint64)
+    r = (((b + 0x7FFF + ((b >> 16) & 1)) >> 16) << 16).astype(np.uint32).view(F32)
+    return np.where(np.isnan(x), x, r).astype(F32)
+
+
+def _h16(x, dtype: str) -> np.ndarray:
+    """Exact float32 values of a 16-bit float input (fp16 arrays, or float32 arrays
+    holding bf16 values)."""
+    if dtype == "float16":
+        return np.asarray(x, dtype=np.float16).astype(F32)
+    if dtype == "bfloat16":
+        return bf16_round(np.asarray(x, dtype=F32))
+    raise ValueError(f"dtype must be float16 or bfloat16, got {dtype}")
+
+
+def _meta(x: np.ndarray, dtype: str) -> np.ndarray:
+    """A float32 scale / zero-point as stored in the cache: fp16, or fp16 then bf16."""
+    h = np.asarray(x, dtype=F32).astype(np.float16)
+    return h if dtype == "float16" else bf16_round(h.astype(F32))
 
 
 # ---------------------------------------------------------------------------
@@ -73,14 +106,16 @@ def _clamp_range(r: np.ndarray) -> np.ndarray:
 # key quantisation (per channel, INT4 for boosted channels, INT2 otherwise)
 # ---------------------------------------------------------------------------
 
-def quantize_key_page(key: np.ndarray, boost_idx: np.ndarray, d_boost: int,
-                      sentinel: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
+def quantize_key_page(key: np.ndarray, boost_idx: np.ndarray, d_boost: int, sentinel: int, dtype: str = "float16",
+                      meta_dtype: str = None) -> Tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
     """Restates ``quantize_key_page_torch`` (``quantize_key.py:38-124``).
 
     key: (D, G) float16, boost_idx: (D,) uint8.  Returns
-    (low (D, G/4) u8, high (d_boost, G/4) u8, scale (D,) f16, zero (D,) f16).
+    (low (D, G/4) u8, high (d_boost, G/4) u8, scale (D,) f16, zero (D,) f16)
+    (bf16 values as float32 with ``dtype="bfloat16"``; ``meta_dtype="float16"`` gives
+    the fp16 scale / zero-point the functional form returns for a bf16 input).
     """
-    x = np.asarray(key, dtype=np.float16).astype(F32)
+    x = _h16(key, dtype)
     D, G = x.shape
     assert G % 4 == 0
     bidx = np.asarray(boost_idx).astype(np.int64)
@@ -103,11 +138,12 @@ def quantize_key_page(key: np.ndarray, boost_idx: np.ndarray, d_boost: int,
         r = int(bidx[c])
         if r < d_boost:
             high[r] |= packed_high[c]
-    return low, high, scale.astype(np.float16), zp.astype(np.float16)
+    m = meta_dtype or dtype
+    return low, high, _meta(scale, m), _meta(zp, m)
 
 
 def dequantize_key_page(low: np.ndarray, high: np.ndarray, scale: np.ndarray,
-                        zero: np.ndarray, boost_idx: np.ndarray, d_boost: int) -> np.ndarray:
+                        zero: np.ndarray, boost_idx: np.ndarray, d_boost: int, dtype: str = "float16") -> np.ndarray:
     """Restates ``dequantize_key_page_torch`` (``dequantize_key.py:35-97``): (D, G) float32."""
     D, G4 = low.shape
     code = unpack_2bit(low).astype(np.int32)                        # :70-74
@@ -117,8 +153,8 @@ def dequantize_key_page(low: np.ndarray, high: np.ndarray, scale: np.ndarray,
         if bidx[c] < d_boost:
             hi[c] = unpack_2bit(high[bidx[c]]).astype(np.int32)
     xq = (code | (hi << 2)).astype(F32)                             # :90
-    s = np.asarray(scale, dtype=np.float16).astype(F32)[:, None]
-    z = np.asarray(zero, dtype=np.float16).astype(F32)[:, None]
+    s = _h16(scale, dtype)[:, None]
+    z = _h16(zero, dtype)[:, None]
     return ((xq - z) * s).astype(F32)                               # :93-95
 
 
@@ -126,12 +162,13 @@ def dequantize_key_page(low: np.ndarray, high: np.ndarray, scale: np.ndarray,
 # value quantisation (per token INT2)
 # ---------------------------------------------------------------------------
 
-def quantize_value_page(value: np.ndarray) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+def quantize_value_page(value: np.ndarray, dtype: str = "float16",
+                        meta_dtype: str = None) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
     """Restates ``quantize_value_page_torch`` (``quantize_value.py:38-90``).
 
     value: (G, D) float16.  Returns (codes (G, D/4) u8, scale (G,) f16, zero (G,) f16).
     """
-    v = np.asarray(value, dtype=np.float16).astype(F32)
+    v = _h16(value, dtype)
     v_min = v.min(axis=1)                                           # :62
     v_max = v.max(axis=1)                                           # :63
     v_range = _clamp_range((v_max - v_min).astype(F32))             # :64
@@ -141,14 +178,16 @@ def quantize_value_page(value: np.ndarray) -> Tuple[np.ndarray, np.ndarray, np.n
     vq = (np.rint((v / scale[:, None]).astype(F32)) + zp[:, None]).astype(F32)   # :77
     vq = np.minimum(np.maximum(vq, F32(0.0)), F32(3.0))             # :78-81
     codes = np.nan_to_num(vq, nan=0.0).astype(np.uint8)
-    return pack_2bit(codes), scale.astype(np.float16), zp.astype(np.float16)
+    m = meta_dtype or dtype
+    return pack_2bit(codes), _meta(scale, m), _meta(zp, m)
 
 
-def dequantize_value_page(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray) -> np.ndarray:
+def dequantize_value_page(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray,
+                          dtype: str = "float16") -> np.ndarray:
     """Restates ``dequantize_value_page_torch`` (``quantize_value.py:97-133``): (G, D) float32."""
     code = unpack_2bit(packed).astype(F32)
-    s = np.asarray(scale, dtype=np.float16).astype(F32)[:, None]
-    z = np.asarray(zero, dtype=np.float16).astype(F32)[:, None]
+    s = _h16(scale, dtype)[:, None]
+    z = _h16(zero, dtype)[:, None]
     return ((code - z) * s).astype(F32)
 
 
@@ -157,13 +196,13 @@ def dequantize_value_page(packed: np.ndarray, scale: np.ndarray, zero: np.ndarra
 # ---------------------------------------------------------------------------
 
 def quantize_key_pages(keys: np.ndarray, boost_idx: np.ndarray, d_boost: int,
-                       sentinel: int) -> Tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
+                       sentinel: int, dtype: str = "float16") -> Tuple[np.ndarray, np.ndarray, np.ndarray, np.ndarray]:
     """Batch of :func:`quantize_key_page` over leading axes.
 
     keys: (..., D, G) float16; boost_idx broadcastable to (..., D).
     Identical arithmetic to the single-page form (checked in the tests).
     """
-    x = np.asarray(keys, dtype=np.float16).astype(F32)
+    x = _h16(keys, dtype)
     lead = x.shape[:-2]
     D, G = x.shape[-2:]
     bidx = np.broadcast_to(np.asarray(boost_idx).astype(np.int64), lead + (D,))
@@ -190,12 +229,12 @@ def quantize_key_pages(keys: np.ndarray, boost_idx: np.ndarray, d_boost: int,
         # OR the channel's high plane into row boost_idx[c] where selected
         idx = np.nonzero(sel)
         high[idx + (rows[idx],)] |= packed_high[idx + (c,)]
-    return low, high, scale.astype(np.float16), zp.astype(np.float16)
+    return low, high, _meta(scale, dtype), _meta(zp, dtype)
 
 
-def quantize_value_pages(values: np.ndarray) -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
+def quantize_value_pages(values: np.ndarray, dtype: str = "float16") -> Tuple[np.ndarray, np.ndarray, np.ndarray]:
     """Batch of :func:`quantize_value_page`; values: (..., G, D) float16."""
-    v = np.asarray(values, dtype=np.float16).astype(F32)
+    v = _h16(values, dtype)
     v_min = v.min(axis=-1)
     v_max = v.max(axis=-1)
     v_range = _clamp_range((v_max - v_min).astype(F32))
@@ -205,11 +244,11 @@ def quantize_value_pages(values: np.ndarray) -> Tuple[np.ndarray, np.ndarray, np
     vq = (np.rint((v / scale[..., None]).astype(F32)) + zp[..., None]).astype(F32)
     vq = np.minimum(np.maximum(vq, F32(0.0)), F32(3.0))
     codes = np.nan_to_num(vq, nan=0.0).astype(np.uint8)
-    return pack_2bit(codes), scale.astype(np.float16), zp.astype(np.float16)
+    return pack_2bit(codes), _meta(scale, dtype), _meta(zp, dtype)
 
 
 def dequantize_key_pages(low: np.ndarray, high: np.ndarray, scale: np.ndarray,
-                         zero: np.ndarray, boost_idx: np.ndarray, d_boost: int) -> np.ndarray:
+                         zero: np.ndarray, boost_idx: np.ndarray, d_boost: int, dtype: str = "float16") -> np.ndarray:
     """Batch of :func:`dequantize_key_page`; low (..., D, G/4) -> (..., D, G) float32."""
     code = unpack_2bit(low).astype(np.int32)
     lead = low.shape[:-2]
@@ -222,16 +261,17 @@ def dequantize_key_pages(low: np.ndarray, high: np.ndarray, scale: np.ndarray,
         gathered = np.take_along_axis(hi_all, rows[..., None], axis=-2)
         hi = np.where((bidx < d_boost)[..., None], gathered, 0)
     xq = (code | (hi << 2)).astype(F32)
-    s = np.asarray(scale, dtype=np.float16).astype(F32)[..., None]
-    z = np.asarray(zero, dtype=np.float16).astype(F32)[..., None]
+    s = _h16(scale, dtype)[..., None]
+    z = _h16(zero, dtype)[..., None]
     return ((xq - z) * s).astype(F32)
 
 
-def dequantize_value_pages(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray) -> np.ndarray:
+def dequantize_value_pages(packed: np.ndarray, scale: np.ndarray, zero: np.ndarray,
+                           dtype: str = "float16") -> np.ndarray:
     """Batch of :func:`dequantize_value_page`; (..., G, D/4) -> (..., G, D) float32."""
     code = unpack_2bit(packed).astype(F32)
-    s = np.asarray(scale, dtype=np.float16).astype(F32)[..., None]
-    z = np.asarray(zero, dtype=np.float16).astype(F32)[..., None]
+    s = _h16(scale, dtype)[..., None]
+    z = _h16(zero, dtype)[..., None]
     return ((code - z) * s).astype(F32)
 
 
@@ -244,7 +284,7 @@ def paged_attention(q: np.ndarray, page_list: Sequence[int], key_baseline: np.nd
                     value_meta: np.ndarray, boost_idx: np.ndarray, d_boost: int,
                     sink_k: np.ndarray, sink_v: np.ndarray, qbuf_k: np.ndarray,
                     qbuf_v: np.ndarray, num_q_heads: int, num_kv_heads: int,
-                    head_dim: int) -> np.ndarray:
+                    head_dim: int, dtype: str = "float16") -> np.ndarray:
     """Restates ``paged_attention_reference`` (``kitty/kernels/attention.py:46-189``).
 
     Per KV head the keys are [sinks ; dequantised pages in ``page_list`` order ;
@@ -262,24 +302,24 @@ def paged_attention(q: np.ndarray, page_list: Sequence[int], key_baseline: np.nd
     for h in range(H):
         kp, vp = [], []
         if sink_k.shape[1] > 0:
-            kp.append(np.asarray(sink_k[h], dtype=np.float16).astype(F32))
-            vp.append(np.asarray(sink_v[h], dtype=np.float16).astype(F32))
+            kp.append(_h16(sink_k[h], dtype))
+            vp.append(_h16(sink_v[h], dtype))
         if pages:
             pidx = np.asarray(pages, dtype=np.int64)
             kdq = dequantize_key_pages(key_baseline[pidx, h], key_boost[pidx, h],
                                        key_meta[pidx, h, 0], key_meta[pidx, h, 1],
-                                       boost_idx[h], d_boost)          # (n, D, G)
+                                       boost_idx[h], d_boost, dtype)   # (n, D, G)
             kp.append(np.swapaxes(kdq, 1, 2).reshape(-1, D))
             vdq = dequantize_value_pages(value_pool[pidx, h], value_meta[pidx, h, :, 0],
-                                         value_meta[pidx, h, :, 1])     # (n, G, D)
+                                         value_meta[pidx, h, :, 1], dtype)   # (n, G, D)
             vp.append(vdq.reshape(-1, D))
         if qbuf_k.shape[1] > 0:                                        # :163
-            kp.append(np.asarray(qbuf_k[h], dtype=np.float16).astype(F32))
-            vp.append(np.asarray(qbuf_v[h], dtype=np.float16).astype(F32))
+            kp.append(_h16(qbuf_k[h], dtype))
+            vp.append(_h16(qbuf_v[h], dtype))
         keys_h.append(np.concatenate(kp, axis=0) if kp else np.zeros((0, D), F32))
         vals_h.append(np.concatenate(vp, axis=0) if vp else np.zeros((0, D), F32))
     scale_factor = F32(1.0 / math.sqrt(D))
-    qf = np.asarray(q, dtype=np.float16).astype(F32)
+    qf = _h16(q, dtype)
     out = np.zeros((num_q_heads, D), dtype=F32)
     for qh in range(num_q_heads):
         K = keys_h[qh // q_per_kv]
@@ -299,7 +339,8 @@ def paged_attention(q: np.ndarray, page_list: Sequence[int], key_baseline: np.nd
 def paged_attention_batched(q: np.ndarray, block_table: np.ndarray, num_pages: np.ndarray,
                             pools: Tuple[np.ndarray, ...], boost_idx: np.ndarray, d_boost: int,
                             sink_k: np.ndarray, sink_v: np.ndarray, sink_len: np.ndarray,
-                            tail_k: np.ndarray, tail_v: np.ndarray, tail_len: np.ndarray) -> np.ndarray:
+                            tail_k: np.ndarray, tail_v: np.ndarray, tail_len: np.ndarray,
+                            dtype: str = "float16") -> np.ndarray:
     """Per-sequence application of :func:`paged_attention` (the reference is batch 1,
     ``kitty/attention.py:100``; a batch is B independent calls).
 
@@ -314,7 +355,7 @@ def paged_attention_batched(q: np.ndarray, block_table: np.ndarray, num_pages: n
         out[b] = paged_attention(q[b], block_table[b, :n], key_low, key_high, key_meta,
                                  val_codes, val_meta, boost_idx, d_boost,
                                  sink_k[b, :, :s], sink_v[b, :, :s], tail_k[b, :, :t],
-                                 tail_v[b, :, :t], Hq, H, D)
+                                 tail_v[b, :, :t], Hq, H, D, dtype)
     return out
 
 
@@ -333,13 +374,16 @@ def cache_regions(n_tokens: int, sink_size: int, group: int) -> Tuple[int, int, 
 
 
 def sequence_state(keys: np.ndarray, values: np.ndarray, sink_size: int, group: int,
-                   boost_idx: np.ndarray, d_boost: int, sentinel: int) -> dict:
+                   boost_idx: np.ndarray, d_boost: int, sentinel: int, dtype: str = "float16") -> dict:
     """Expected cache contents of one sequence whose tokens are keys / values (T, H, D)
     float16: fp16 sinks and tail, and for each page the quantised key planes (of the
     (H, D, G) block of its G keys) and value planes (of its G values, the values of
     the same tokens - the pipeline's aligned-values mode)."""
-    keys = np.asarray(keys, np.float16)
-    values = np.asarray(values, np.float16)
+    if dtype == "float16":
+        keys = np.asarray(keys, np.float16)
+        values = np.asarray(values, np.float16)
+    else:
+        keys, values = _h16(keys, dtype), _h16(values, dtype)
     s, n, t = cache_regions(keys.shape[0], sink_size, group)
     out = {"sink_k": keys[:s].transpose(1, 0, 2), "sink_v": values[:s].transpose(1, 0, 2),
            "tail_k": keys[s + n * group:].transpose(1, 0, 2), "tail_v": values[s + n * group:].transpose(1, 0, 2),
@@ -347,8 +391,8 @@ def sequence_state(keys: np.ndarray, values: np.ndarray, sink_size: int, group: 
     for j in range(n):
         kb = keys[s + j * group: s + (j + 1) * group]          # (G, H, D)
         vb = values[s + j * group: s + (j + 1) * group]
-        low, high, scale, zero = quantize_key_pages(kb.transpose(1, 2, 0), boost_idx, d_boost, sentinel)
-        codes, vscale, vzero = quantize_value_pages(vb.transpose(1, 0, 2))
+        low, high, scale, zero = quantize_key_pages(kb.transpose(1, 2, 0), boost_idx, d_boost, sentinel, dtype)
+        codes, vscale, vzero = quantize_value_pages(vb.transpose(1, 0, 2), dtype)
         out["pages"].append({"key_low": low, "key_high": high, "key_scale": scale, "key_zero": zero,
                              "val_codes": codes, "val_scale": vscale, "val_zero": vzero})
     return out

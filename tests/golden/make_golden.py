@@ -363,13 +363,109 @@ def check_profiler(ref, manifest):
                             "boost_idx_sha": sha(prof.boost_idx_uint8.numpy())}
 
 
+BF16_ATTN = [
+    # bfloat16 cache: same generator, values rounded to bf16 (name, seed, B, Hq, H, D, contexts, sink, group, rate)
+    ("bf16_tiny", 51, 2, 4, 2, 16, [4 + 3 * 8 + 5, 4 + 8 + 2], 4, 8, 0.25),
+    ("bf16_d128", 52, 2, 8, 2, 128, [32 + 2 * 128 + 17, 32 + 128 + 96], 32, 128, 0.125),
+]
+
+
+def run_bf16_sets(ref, rng, store, manifest):
+    """A bfloat16 cache (KittyConfig(dtype="bfloat16")): the reference launchers write
+    into bf16 pool views through their CPU branch (quantize_key.py:261-269,
+    quantize_value.py:223-227), so the stored scale / zero-point are the fp16 results
+    converted to bf16; dequantisation and attention read everything with .float()."""
+    from kitty_ref.kernels import (quantize_key_page, quantize_value_page, dequantize_key_page_torch,
+                                   dequantize_value_page_torch, paged_attention_reference)
+    bf = torch.bfloat16
+    names = []
+    for name, key, bidx, K, sent in small_key_cases(rng):
+        kb = torch.from_numpy(key.astype(np.float32)).to(bf)
+        D, G = key.shape
+        low = torch.zeros(D, G // 4, dtype=torch.uint8); high = torch.zeros(K, G // 4, dtype=torch.uint8)
+        meta = torch.zeros(2, D, dtype=bf)
+        quantize_key_page(kb, torch.from_numpy(bidx), K, sent, low, high, meta[0], meta[1])
+        rec = dequantize_key_page_torch(low, high, meta[0], meta[1], torch.from_numpy(bidx), K)
+        p = f"bf16key/{name}/"
+        store[p + "key"] = kb.float().numpy()
+        store[p + "boost_idx"] = bidx
+        store[p + "params"] = np.array([K, sent], np.int64)
+        store[p + "low"] = low.numpy(); store[p + "high"] = high.numpy()
+        store[p + "scale"] = meta[0].float().numpy(); store[p + "zero"] = meta[1].float().numpy()
+        store[p + "dequant"] = rec.numpy()
+        names.append(("bf16key", name))
+    for name, val in small_value_cases(rng):
+        vb = torch.from_numpy(val.astype(np.float32)).to(bf)
+        G, D = val.shape
+        packed = torch.zeros(G, D // 4, dtype=torch.uint8)
+        vmeta = torch.zeros(G, 2, dtype=bf)
+        quantize_value_page(vb, packed, vmeta[:, 0], vmeta[:, 1])
+        rec = dequantize_value_page_torch(packed, vmeta[:, 0], vmeta[:, 1])
+        p = f"bf16value/{name}/"
+        store[p + "value"] = vb.float().numpy()
+        store[p + "codes"] = packed.numpy()
+        store[p + "scale"] = vmeta[:, 0].float().numpy(); store[p + "zero"] = vmeta[:, 1].float().numpy()
+        store[p + "dequant"] = rec.numpy()
+        names.append(("bf16value", name))
+    manifest["bf16_small"] = names
+    manifest["bf16_attention"] = {}
+    for name, seed, B, Hq, H, D, ctx, S, G, rate in BF16_ATTN:
+        case = synthetic.make_decode_case(seed, B, Hq, H, D, ctx, sink=S, group=G, boost_rate=rate)
+        phys_of, n_phys = phys_layout(case, seed + 1000)
+        K = case.d_boost
+        kl = torch.zeros(n_phys, H, D, G // 4, dtype=torch.uint8)
+        kh = torch.zeros(n_phys, H, K, G // 4, dtype=torch.uint8)
+        km = torch.zeros(n_phys, H, 2, D, dtype=bf)
+        vc = torch.zeros(n_phys, H, G, D // 4, dtype=torch.uint8)
+        vm = torch.zeros(n_phys, H, G, 2, dtype=bf)
+        bidx = torch.from_numpy(case.boost_idx)
+        outs = []
+        for b, sq in enumerate(case.seqs):
+            pk = sq.page_keys(); pv = sq.page_values()
+            for i in range(sq.n_pages):
+                pg = int(phys_of[b][i])
+                for h in range(H):
+                    quantize_key_page(torch.from_numpy(pk[i, h].astype(np.float32)).to(bf), bidx[h], K, case.sentinel,
+                                      kl[pg, h], kh[pg, h], km[pg, h, 0], km[pg, h, 1])
+                    quantize_value_page(torch.from_numpy(pv[i, h].astype(np.float32)).to(bf), vc[pg, h],
+                                        vm[pg, h, :, 0], vm[pg, h, :, 1])
+        for b, sq in enumerate(case.seqs):
+            sk, sv = sq.sink_kv(); tk, tv = sq.tail_kv()
+            cv = lambda a: torch.from_numpy(a.astype(np.float32)).to(bf)
+            o = paged_attention_reference(
+                q=cv(case.q[b]), page_list=[int(x) for x in phys_of[b][:sq.n_pages]],
+                key_baseline=kl, key_boost=kh, key_meta=km, value_pool=vc, value_meta=vm, boost_idx=bidx,
+                D_boost=K, sink_k=cv(sk), sink_v=cv(sv), qbuf_k=cv(tk), qbuf_v=cv(tv),
+                num_q_heads=case.num_q_heads, num_kv_heads=H, head_dim=D)
+            outs.append(o.numpy())
+        entry = {"seed": seed, "batch": B, "num_q_heads": Hq, "num_kv_heads": H, "head_dim": D, "contexts": ctx,
+                 "sink": S, "group": G, "boost_rate": rate, "phys_seed": seed + 1000, "n_phys": n_phys,
+                 "d_boost": K, "sentinel": case.sentinel,
+                 "pools_sha": {"key_low": sha(kl.numpy()), "key_high": sha(kh.numpy()), "val_codes": sha(vc.numpy()),
+                               "key_meta_value": sha(km.float().numpy() + 0.0),
+                               "val_meta_value": sha(vm.float().numpy() + 0.0)}}
+        store[f"bf16attn/{name}/out"] = np.stack(outs)
+        manifest["bf16_attention"][name] = entry
+        print(f"  bf16 attention {name}", flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference", default=os.environ.get("KITTY_REFERENCE", "/root/reference"))
     ap.add_argument("--skip-quant", action="store_true")
+    ap.add_argument("--bf16-only", action="store_true",
+                    help="add the bfloat16 sets to the existing golden files and keep everything else")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = load_reference(Path(args.reference))
+    if args.bf16_only:
+        with np.load(HERE / "golden_small.npz") as z:
+            store = {k: z[k] for k in z.files}
+        manifest = json.loads((HERE / "golden_manifest.json").read_text())
+        run_bf16_sets(ref, np.random.default_rng(2025), store, manifest)
+        np.savez_compressed(HERE / "golden_small.npz", **store)
+        (HERE / "golden_manifest.json").write_text(json.dumps(manifest, indent=1, default=int))
+        return
     rng = np.random.default_rng(2024)
     store = {}
     manifest = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__,
@@ -378,6 +474,7 @@ def main():
     run_attention_sets(ref, store, manifest)
     run_pipeline_compat(ref, store, manifest)
     check_profiler(ref, manifest)
+    run_bf16_sets(ref, np.random.default_rng(2025), store, manifest)
     if not args.skip_quant:
         run_quant_sets(ref, manifest, store)
     np.savez_compressed(HERE / "golden_small.npz", **store)

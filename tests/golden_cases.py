@@ -39,13 +39,14 @@ def phys_layout(case, seed, n_phys):
     return phys_of
 
 
-def padded_regions(case):
-    """(B, H, S, D) sinks, (B, H, Q, D) tails (zero padded) and their lengths."""
+def padded_regions(case, dtype=np.float16):
+    """(B, H, S, D) sinks, (B, H, Q, D) tails (zero padded) and their lengths
+    (float32 arrays of bf16 values for a bfloat16 case)."""
     B, H, D = len(case.seqs), case.num_kv_heads, case.head_dim
     S = max([s.sink for s in case.seqs] + [1])
     Q = max([s.tail for s in case.seqs] + [1])
-    sk = np.zeros((B, H, S, D), np.float16); sv = np.zeros_like(sk)
-    tk = np.zeros((B, H, Q, D), np.float16); tv = np.zeros_like(tk)
+    sk = np.zeros((B, H, S, D), dtype); sv = np.zeros_like(sk)
+    tk = np.zeros((B, H, Q, D), dtype); tv = np.zeros_like(tk)
     for b, s in enumerate(case.seqs):
         a, c = s.sink_kv(); sk[b, :, :s.sink] = a; sv[b, :, :s.sink] = c
         a, c = s.tail_kv(); tk[b, :, :s.tail] = a; tv[b, :, :s.tail] = c
@@ -61,3 +62,16 @@ def block_table(case, phys_of):
     for b, p in enumerate(phys_of):
         bt[b, :len(p)] = p
     return bt, np.array([len(p) for p in phys_of], np.int32)
+
+
+def bf16_case_from_manifest(entry, bf16_round) -> synthetic.DecodeCase:
+    """A recorded bfloat16 decode case: the fp16 generator's keys, values and queries
+    rounded to bf16 (float32 arrays); boost_idx as generated."""
+    case = synthetic.make_decode_case(entry["seed"], entry["batch"], entry["num_q_heads"],
+                                      entry["num_kv_heads"], entry["head_dim"], entry["contexts"],
+                                      sink=entry["sink"], group=entry["group"], boost_rate=entry["boost_rate"])
+    for s in case.seqs:
+        s.k = bf16_round(s.k.astype(np.float32))
+        s.v = bf16_round(s.v.astype(np.float32))
+    case.q = bf16_round(case.q.astype(np.float32))
+    return case

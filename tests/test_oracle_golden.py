@@ -184,3 +184,87 @@ def test_sequence_state_matches_reference_pipeline(golden_npz, golden_manifest, 
     qbuf = np.zeros((1, H, G, D), np.float16)
     qbuf[0, :, :t] = st["tail_k"]
     assert sha(qbuf) == e["buffers_sha"]["key_qbuf"]
+
+
+# ----------------------------------------------------------------- bfloat16 cache
+
+BF16_KEY = ["rand0", "rand1", "rand2", "rand3", "constant_channels", "all_zero", "wide_ranges", "permuted_boost",
+            "duplicate_rows", "boost_eq_k", "known_answer_0123", "halfway", "d128_page"]
+BF16_VALUE = ["rand0", "rand1", "rand2", "constant_3", "all_zero", "constant_rows", "wide_ranges", "halfway",
+              "d128_page"]
+
+
+def test_bf16_sets_are_recorded(golden_manifest):
+    assert sorted(n for k, n in golden_manifest["bf16_small"] if k == "bf16key") == sorted(BF16_KEY)
+    assert sorted(n for k, n in golden_manifest["bf16_small"] if k == "bf16value") == sorted(BF16_VALUE)
+
+
+def test_bf16_round_matches_torch():
+    """bf16_round == torch's float32 -> bfloat16 conversion (ties, overflow, subnormals)."""
+    import torch
+    rng = np.random.default_rng(3)
+    x = np.concatenate([rng.standard_normal(20000).astype(np.float32) * np.float32(10.0) ** rng.integers(-40, 38, 20000),
+                        np.array([1.0, 1.00390625, 1.005859375, 1.0078125, 65504.0, 3.4e38, 3.3e38, np.inf, -np.inf,
+                                  -0.0, 1e-40, -1e-45], np.float32)]).astype(np.float32)
+    exp = torch.from_numpy(x).to(torch.bfloat16).float().numpy()
+    np.testing.assert_array_equal(O.bf16_round(x), exp)
+    assert np.isnan(O.bf16_round(np.array([np.nan], np.float32)))[0]
+
+
+@pytest.mark.parametrize("name", BF16_KEY)
+def test_bf16_key_quantize_matches_reference(golden_npz, name):
+    p = f"bf16key/{name}/"
+    K, sent = (int(x) for x in golden_npz[p + "params"])
+    low, high, sc, zp = O.quantize_key_page(golden_npz[p + "key"], golden_npz[p + "boost_idx"], K, sent,
+                                            dtype="bfloat16")
+    np.testing.assert_array_equal(low, golden_npz[p + "low"])
+    np.testing.assert_array_equal(high, golden_npz[p + "high"])
+    np.testing.assert_array_equal(meta_by_value(sc), meta_by_value(golden_npz[p + "scale"]))
+    np.testing.assert_array_equal(meta_by_value(zp), meta_by_value(golden_npz[p + "zero"]))
+    rec = O.dequantize_key_page(low, high, sc, zp, golden_npz[p + "boost_idx"], K, dtype="bfloat16")
+    np.testing.assert_array_equal(rec, golden_npz[p + "dequant"])
+
+
+@pytest.mark.parametrize("name", BF16_VALUE)
+def test_bf16_value_quantize_matches_reference(golden_npz, name):
+    p = f"bf16value/{name}/"
+    codes, sc, zp = O.quantize_value_page(golden_npz[p + "value"], dtype="bfloat16")
+    np.testing.assert_array_equal(codes, golden_npz[p + "codes"])
+    np.testing.assert_array_equal(meta_by_value(sc), meta_by_value(golden_npz[p + "scale"]))
+    np.testing.assert_array_equal(meta_by_value(zp), meta_by_value(golden_npz[p + "zero"]))
+    np.testing.assert_array_equal(O.dequantize_value_page(codes, sc, zp, dtype="bfloat16"), golden_npz[p + "dequant"])
+
+
+def bf16_oracle_pools(case, phys_of, n_phys):
+    H, D, G, K = case.num_kv_heads, case.head_dim, case.group, case.d_boost
+    kl = np.zeros((n_phys, H, D, G // 4), np.uint8); kh = np.zeros((n_phys, H, K, G // 4), np.uint8)
+    km = np.zeros((n_phys, H, 2, D), np.float32); vc = np.zeros((n_phys, H, G, D // 4), np.uint8)
+    vm = np.zeros((n_phys, H, G, 2), np.float32)
+    for b, s in enumerate(case.seqs):
+        if s.n_pages == 0:
+            continue
+        low, high, sc, zp = O.quantize_key_pages(s.page_keys(), case.boost_idx, K, case.sentinel, dtype="bfloat16")
+        codes, vs, vz = O.quantize_value_pages(s.page_values(), dtype="bfloat16")
+        p = phys_of[b]
+        kl[p] = low; kh[p] = high; km[p, :, 0] = sc; km[p, :, 1] = zp
+        vc[p] = codes; vm[p, :, :, 0] = vs; vm[p, :, :, 1] = vz
+    return kl, kh, km, vc, vm
+
+
+@pytest.mark.parametrize("name", ["bf16_tiny", "bf16_d128"])
+def test_bf16_attention_pools_and_outputs_match_reference(golden_npz, golden_manifest, name):
+    e = golden_manifest["bf16_attention"][name]
+    case = GC.bf16_case_from_manifest(e, O.bf16_round)
+    phys_of = GC.phys_layout(case, e["phys_seed"], e["n_phys"])
+    pools = bf16_oracle_pools(case, phys_of, e["n_phys"])
+    assert sha(pools[0]) == e["pools_sha"]["key_low"]
+    assert sha(pools[1]) == e["pools_sha"]["key_high"]
+    assert sha(pools[3]) == e["pools_sha"]["val_codes"]
+    assert sha(pools[2] + np.float32(0.0)) == e["pools_sha"]["key_meta_value"]
+    assert sha(pools[4] + np.float32(0.0)) == e["pools_sha"]["val_meta_value"]
+    sk, sv, sl, tk, tv, tl = GC.padded_regions(case, np.float32)
+    bt, npg = GC.block_table(case, phys_of)
+    out = O.paged_attention_batched(case.q, bt, npg, pools, case.boost_idx, case.d_boost, sk, sv, sl, tk, tv, tl,
+                                    dtype="bfloat16")
+    np.testing.assert_allclose(out.astype(np.float32), golden_npz[f"bf16attn/{name}/out"].astype(np.float32),
+                               atol=1e-3, rtol=1e-3)
