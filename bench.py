@@ -742,8 +742,9 @@ def quantize_arm(args, spec, d, device, local):
 def decode_kernel_name(variant, g, D, G):
     """Kernel family a decode call runs (the library's choice for "auto")."""
     if variant == "auto":
-        variant = "int8" if (D == 128 and G == 128 and g <= 4) else ("mma" if (D == 128 and G == 128 and g <= 8)
-                                                                      else "simt")
+        variant = "int8" if (D == 128 and G == 128 and g <= 8) else "simt"
+    elif variant == "mma" and not (D == 128 and G == 128 and g <= 8):
+        variant = "int8" if (D == 128 and G == 128 and g <= 8) else "simt"
     return {"int8": "decode_i8_kernel", "mma": "decode_mma_kernel", "simt": "decode_simt_kernel"}[variant]
 
 
@@ -756,8 +757,8 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--variant", choices=["auto", "simt", "mma", "int8"], default="auto",
-                    help="decode kernel family (auto: integer tensor-core kernel for <= 4 query heads per "
-                         "KV head, fp16 tensor-core kernel up to 8, CUDA-core kernel otherwise)")
+                    help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128 "
+                         "and up to 8 query heads per KV head, CUDA-core kernel otherwise)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     spec = WORKLOADS[args.workload]

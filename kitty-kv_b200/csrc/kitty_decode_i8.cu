@@ -73,21 +73,25 @@ constexpr float kKeyRange = 4194300.0f;     // 2^22 - 4: |x| < 2^22 even with an
 constexpr float kValRange = 65535.0f;
 constexpr float kMagicKey = 12582912.0f;    // 1.5 * 2^23: fma(w, R, magic) has bits 0x4B400000 + rint(w R)
 constexpr float kMagicVal = 8388608.0f;     // 2^23: fma(P', Rv, magic) has bits 0x4B000000 + rint(P' Rv)
-constexpr int kPlane = 656;                 // digit table: plane stride (bytes; 164 words = 4 mod 32 banks)
 constexpr int kRow = 160;                   // digit table: query-head row stride (bytes; 40 words = 8 mod 32)
+// digit table plane stride for 4 (8) query-head rows: 164 (324) words = 4 mod 32 banks
+__host__ __device__ constexpr int plane_bytes(int qg) { return qg == 1 ? 656 : 1296; }
+constexpr int kCtasPerSmG8 = 2;              // resident CTAs per SM of the 8-query-head kernel
 constexpr int kPhRow = 136;                 // fp16 P staging (fp16 region): row stride in halves
 
 // per-warp shared memory (bytes)
 struct Layout {
-  int kbuf, vbuf, dtab, ptab, ent, bars, size;
+  int kbuf, vbuf, dtab, ptab, ent, bars, size, plane;
 };
-__host__ __device__ inline Layout i8_layout(int K) {
+// qg = groups of four query heads per KV head (1: g <= 4, 2: g <= 8)
+__host__ __device__ inline Layout i8_layout(int K, int qg) {
   Layout L;
+  L.plane = plane_bytes(qg);
   int o = 0;
   L.kbuf = o; o += (4096 + 512 + K * 32 + 32 + 127) & ~127;  // low plane, scale/zero rows, high plane, zero row
   L.vbuf = o; o += 4096 + 512;                               // codes, (scale, zero) per token
-  L.dtab = o; o += 3 * kPlane;                               // key digits b0, b1, b2 [qh][channel]
-  L.ptab = o; o += 2 * kPlane;                               // P' digits y0, y1 [qh][token] / fp16 P (fp16 region)
+  L.dtab = o; o += 3 * L.plane;                              // key digits b0, b1, b2 [qh][channel]
+  L.ptab = o; o += 2 * L.plane;                              // P' digits y0, y1 [qh][token] / fp16 P (fp16 region)
   L.ent = o;  o += 128 * 4;                                  // boosted entries (row offset | position << 16)
   L.bars = o; o += 16;
   L.size = (o + 127) & ~127;
@@ -271,20 +275,24 @@ __device__ __forceinline__ void softmax_step(State& st, float (&s)[16]) {
   st.l += sum.x + sum.y;
 }
 
-// Per-segment setup: q of the prep lane's (query head, 16 channels) and the
+// Per-segment setup: q of the prep lane's (query heads pq + 4 qg, 16 channels) and the
 // boosted-entry table.  Returns the number of boosted entries.
+template <int kQG>
 __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint8_t* wsm, const Layout& L,
-                             int lane, uint32_t (&qreg)[8]) {
+                             int lane, uint32_t (&qreg)[kQG][8]) {
   const int pq = lane >> 3, cb = lane & 7;
-  if (pq < g) {
-    const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
-                                                      int64_t(h * g + pq) * a.q_s_head + 16 * cb);
-    const uint4 x0 = src[0], x1 = src[1];
-    qreg[0] = x0.x; qreg[1] = x0.y; qreg[2] = x0.z; qreg[3] = x0.w;
-    qreg[4] = x1.x; qreg[5] = x1.y; qreg[6] = x1.z; qreg[7] = x1.w;
-  } else {
 #pragma unroll
-    for (int i = 0; i < 8; ++i) qreg[i] = 0u;
+  for (int qg = 0; qg < kQG; ++qg) {
+    if (pq + 4 * qg < g) {
+      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
+                                                        int64_t(h * g + pq + 4 * qg) * a.q_s_head + 16 * cb);
+      const uint4 x0 = src[0], x1 = src[1];
+      qreg[qg][0] = x0.x; qreg[qg][1] = x0.y; qreg[qg][2] = x0.z; qreg[qg][3] = x0.w;
+      qreg[qg][4] = x1.x; qreg[qg][5] = x1.y; qreg[qg][6] = x1.z; qreg[qg][7] = x1.w;
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) qreg[qg][i] = 0u;
+    }
   }
   uint32_t* ent = reinterpret_cast<uint32_t*>(wsm + L.ent);
   const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
@@ -305,14 +313,15 @@ __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint
   return nb;
 }
 
-// Tokens [t_begin, t_end) of the fp16 region of (b, h) (sinks then tail; one chunk
+// Query heads qoff .. qoff + 3, tokens [t_begin, t_end) of the fp16 region of (b, h) (sinks then tail; one chunk
 // item of the segment walk), at most 128 per pass (fp16 MMAs; 16-token tiles without
 // real tokens are skipped).  Scores: token 16 m + g_ + 8 hh <-> row g_ + 8 hh of M tile
 // m; values: channel 32 (m >> 1) + 4 g_ + 2 (m & 1) + hh <-> row g_ + 8 hh of M tile m
 // (the channels of st.o[2 m + hh], as on the page path).
 template <bool kBf16>
-__device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, State& st, uint8_t* wsm,
-                                    const Layout& L, float qk_scale, int lane, int t_begin, int t_end) {
+__device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int g, int qoff, State& st,
+                                    uint8_t* wsm, const Layout& L, float qk_scale, int lane, int t_begin,
+                                    int t_end) {
   const int cr = cache_row(a, b);   // cache row (sinks, tail, lengths)
   const int g_ = lane >> 2, q_ = lane & 3;
   const int sink_len = a.sink_len ? a.sink_len[cr] : a.sink_len_all;
@@ -323,7 +332,7 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
   // index (2q_, 2q_+1, 2q_+8, 2q_+9) of k-step s <-> channel 32 q_ + 4 s + (0..3)
   uint32_t qw[16];
   {
-    const int qh = g_ >> 1;
+    const int qh = qoff + (g_ >> 1);
     if (qh < g) {
       const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
                                                         int64_t(h * g + qh) * a.q_s_head + 32 * q_);
@@ -449,8 +458,12 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
   }
 }
 
-template <bool kBf16>
-__global__ void __launch_bounds__(kThreads, kCtasPerSm)
+// kQG groups of four query heads per KV head share each page-head's unpacked
+// operands: with kQG = 2 the key contraction runs one 64-token half at a time
+// (four accumulator sets: two groups x (byte 1, byte 0 | byte 2, code sum)) and the
+// value contraction one 64-channel half at a time.
+template <bool kBf16, int kQG>
+__global__ void __launch_bounds__(kThreads, kQG == 1 ? kCtasPerSm : kCtasPerSmG8)
 decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   using T = Half16<kBf16>;
   extern __shared__ __align__(128) uint8_t smem[];
@@ -459,7 +472,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g_ = lane >> 2, q_ = lane & 3;
   const int pq = lane >> 3, cb = lane & 7;
-  const Layout L = i8_layout(K);
+  const Layout L = i8_layout(K, kQG);
+  const int kPlane = L.plane;
   uint8_t* wsm = smem + warp * L.size;
   uint8_t* kbuf = wsm + L.kbuf;
   uint8_t* vbuf = wsm + L.vbuf;
@@ -523,10 +537,11 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   if (lane == 0 && have_next) { issue_k(cur); issue_v(cur); }
   __syncwarp();
 
-  State st;
-  reset_state(st);
-  uint32_t qreg[8];
-  int nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane, qreg);
+  State st[kQG];
+#pragma unroll
+  for (int qg = 0; qg < kQG; ++qg) reset_state(st[qg]);
+  uint32_t qreg[kQG][8];
+  int nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane, qreg);
 
   // ldmatrix row addresses: row `lane` of a 32-row k-step of the key / value plane
   const uint32_t k_row = smem_u32(kbuf) + 32u * lane, v_row = smem_u32(vbuf) + 32u * lane;
@@ -541,7 +556,9 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (pos.p < pos.n16) {
       int t0, t1;
       fp16_chunk(fp16_tokens(a, pos.s), pos.n16, pos.p, t0, t1);
-      process_fp16_region<kBf16>(a, b, h, g, st, wsm, L, qk_scale, lane, t0, t1);
+#pragma unroll
+      for (int qg = 0; qg < kQG; ++qg)
+        process_fp16_region<kBf16>(a, b, h, g, 4 * qg, st[qg], wsm, L, qk_scale, lane, t0, t1);
     } else {
       const int64_t page = phys(pos.s, pos.p, pos.n16);
       const bool valid = page >= 0 && page < a.pool_pages;
@@ -550,28 +567,29 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       const uint8_t* km = kbuf + 4096;   // scale[128] fp16, zero[128] fp16
       const uint8_t* kh = kbuf + 4608;   // high plane rows, then the zero row
 
-      // ---- key digits: prep lane (query head pq, channels 16 cb .. 16 cb + 15)
-      float zsum;
-      float delta;
-      {
-        const uint4* sp = reinterpret_cast<const uint4*>(km + 32 * cb);
-        const uint4* zp = reinterpret_cast<const uint4*>(km + 256 + 32 * cb);
-        const uint4 s0 = sp[0], s1 = sp[1], z0 = zp[0], z1 = zp[1];
-        const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
-        const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+      // ---- key digits: prep lane (query heads pq + 4 qg, channels 16 cb .. 16 cb + 15)
+      float zsum[kQG];
+      float delta[kQG];
+      const uint4* sp = reinterpret_cast<const uint4*>(km + 32 * cb);
+      const uint4* zp = reinterpret_cast<const uint4*>(km + 256 + 32 * cb);
+      const uint4 s0 = sp[0], s1 = sp[1], z0 = zp[0], z1 = zp[1];
+      const uint32_t sw[8] = {s0.x, s0.y, s0.z, s0.w, s1.x, s1.y, s1.z, s1.w};
+      const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
+#pragma unroll
+      for (int qg = 0; qg < kQG; ++qg) {
         float w[16];
         float mx = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          w[2 * j] = mul_h16_f32<kBf16>(uint16_t(qreg[j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
-          w[2 * j + 1] = mul_h16_f32<kBf16>(uint16_t(qreg[j] >> 16), uint16_t(sw[j] >> 16));
+          w[2 * j] = mul_h16_f32<kBf16>(uint16_t(qreg[qg][j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
+          w[2 * j + 1] = mul_h16_f32<kBf16>(uint16_t(qreg[qg][j] >> 16), uint16_t(sw[j] >> 16));
           mx = fmaxf(mx, fmaxf(fabsf(w[2 * j]), fabsf(w[2 * j + 1])));
         }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
         const float R = mx > 0.f ? __fdividef(kKeyRange, mx) : 0.f;
-        delta = mx * (1.0f / kKeyRange);
+        delta[qg] = mx * (1.0f / kKeyRange);
         uint32_t fb[16];
         float2 zs2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -582,10 +600,11 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           fb[2 * j + 1] = __float_as_uint(f.y);
           zs2 = fma2(T::to_f2(zw[j]), wj, zs2);
         }
-        zsum = zs2.x + zs2.y;
-        zsum += __shfl_xor_sync(0xffffffffu, zsum, 1);
-        zsum += __shfl_xor_sync(0xffffffffu, zsum, 2);
-        zsum += __shfl_xor_sync(0xffffffffu, zsum, 4);
+        float zsm = zs2.x + zs2.y;
+        zsm += __shfl_xor_sync(0xffffffffu, zsm, 1);
+        zsm += __shfl_xor_sync(0xffffffffu, zsm, 2);
+        zsm += __shfl_xor_sync(0xffffffffu, zsm, 4);
+        zsum[qg] = zsm;
         // word qq <-> channels 16 cb + 4 qq .. 16 cb + 4 qq + 3
         uint32_t d0[4], d1[4], d2[4];
 #pragma unroll
@@ -593,16 +612,24 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           bytes01(fb[4 * qq], fb[4 * qq + 1], fb[4 * qq + 2], fb[4 * qq + 3], d0[qq], d1[qq]);
           d2[qq] = byte2(fb[4 * qq], fb[4 * qq + 1], fb[4 * qq + 2], fb[4 * qq + 3]);
         }
-        uint8_t* row = dtab + pq * kRow + 16 * cb;
+        uint8_t* row = dtab + (pq + 4 * qg) * kRow + 16 * cb;
         *reinterpret_cast<uint4*>(row) = make_uint4(d0[0], d0[1], d0[2], d0[3]);
         *reinterpret_cast<uint4*>(row + kPlane) = make_uint4(d1[0], d1[1], d1[2], d1[3]);
         *reinterpret_cast<uint4*>(row + 2 * kPlane) = make_uint4(d2[0], d2[1], d2[2], d2[3]);
       }
       __syncwarp();
-      // this lane's query head q_: zero-point term and digit step, from prep lane 8 q_
-      const float zq = __shfl_sync(0xffffffffu, zsum, 8 * q_) * qk_scale;
-      const float cq = __shfl_sync(0xffffffffu, delta, 8 * q_) * qk_scale;
-
+      // this lane's query heads q_ + 4 qg: zero-point term and digit step, from prep lane 8 q_
+      float zqg[kQG], cqg[kQG];
+#pragma unroll
+      for (int qg = 0; qg < kQG; ++qg) {
+        zqg[qg] = __shfl_sync(0xffffffffu, zsum[qg], 8 * q_) * qk_scale;
+        cqg[qg] = __shfl_sync(0xffffffffu, delta[qg], 8 * q_) * qk_scale;
+      }
+      // ---- scores (log2 domain): s[qg][4 k + i] <-> token 32 k + 4 g_ + i; tile 4 half + i
+      // holds tokens 64 half + 4 g_ + i (row g_, k = 2 half) and + 32 (row g_ + 8)
+      float s[kQG][16];
+      if constexpr (kQG == 1) {
+      const float zq = zqg[0], cq = cqg[0];
       int acc1[8][4], acc2[8][4];
       // ---- baseline plane
       key_kstep<true>(acc1, acc2, k_row, kb1, kb2, ones_col, 0, q_);
@@ -635,14 +662,6 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           mma_k16(acc2[4 * half + 3], high_code<3>(x0), high_code<3>(x1), bb2);
         }
       }
-      __syncwarp();
-      // keys consumed: request the next page's keys
-      have_next = cursor_step(cur, a) && cursor_to_page(cur, a, f1);
-      if (lane == 0 && have_next) issue_k(cur);
-
-      // ---- scores (log2 domain): s[4 k + i] <-> token 32 k + 4 g_ + i; tile 4 half + i
-      // holds tokens 64 half + 4 g_ + i (row g_, k = 2 half) and + 32 (row g_ + 8)
-      float s[16];
       {
         // row factors 1, 4, 16, 16 of code i
 #pragma unroll
@@ -654,15 +673,98 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           const int hi0 = acc2[mt][0] - 64 * acc2[mt][1], hi1 = acc2[mt][2] - 64 * acc2[mt][3];
           const float2 t = fma2(make_float2(float(lo0), float(lo1)), fl, make_float2(-zq, -zq));
           const float2 r = fma2(make_float2(float(hi0), float(hi1)), fh, t);
-          s[8 * half + i] = r.x;
-          s[8 * half + 4 + i] = r.y;
+          s[0][8 * half + i] = r.x;
+          s[0][8 * half + 4 + i] = r.y;
         }
       }
+      } else {
+        // two query groups, one 64-token half at a time
+        const uint8_t* kb1g[2] = {kb1, kb1 + 4 * kRow};
+        const uint8_t* kb2g[2] = {kb2, kb2 + 4 * kRow};
+#pragma unroll
+        for (int half = 0; half < 2; ++half) {
+          int a1[2][4][4], a2[2][4][4];
+#pragma unroll
+          for (int ks = 0; ks < 4; ++ks) {
+            uint32_t b1[2][2], b2[2][2];
+#pragma unroll
+            for (int qg = 0; qg < 2; ++qg) {
+              b1[qg][0] = lds32(kb1g[qg] + 32 * ks + 4 * q_);
+              b1[qg][1] = lds32(kb1g[qg] + 32 * ks + 16 + 4 * q_);
+              b2[qg][0] = ones_col ? 0x01010101u : lds32(kb2g[qg] + 32 * ks + 4 * q_);
+              b2[qg][1] = ones_col ? 0x01010101u : lds32(kb2g[qg] + 32 * ks + 16 + 4 * q_);
+            }
+            uint32_t r[4];
+            ldsm_t_x2(k_row + 1024u * ks + 16u * half, r);
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t m = i < 3 ? (0x03030303u << (2 * i)) : 0x30303030u;
+              const int sh = i < 3 ? 0 : 2;
+              const uint32_t c0 = (r[0] >> sh) & m, c1 = (r[1] >> sh) & m, c2 = (r[2] >> sh) & m,
+                             c3 = (r[3] >> sh) & m;
+#pragma unroll
+              for (int qg = 0; qg < 2; ++qg) {
+                if (ks == 0) {
+                  mma_k32_z(a1[qg][i], c0, c1, c2, c3, b1[qg][0], b1[qg][1]);
+                  mma_k32_z(a2[qg][i], c0, c1, c2, c3, b2[qg][0], b2[qg][1]);
+                } else {
+                  mma_k32(a1[qg][i], c0, c1, c2, c3, b1[qg][0], b1[qg][1]);
+                  mma_k32(a2[qg][i], c0, c1, c2, c3, b2[qg][0], b2[qg][1]);
+                }
+              }
+            }
+          }
+          for (int bs = 0; bs < nb; bs += 16) {
+            const uint4 e4 = *reinterpret_cast<const uint4*>(ent + bs + 4 * q_);
+            const uint32_t es[4] = {e4.x, e4.y, e4.z, e4.w};
+            uint32_t r[4], bb1[2] = {0u, 0u}, bb2[2] = {0u, 0u};
+            ldsm_t_x2(smem_u32(kh) + (ent[bs + (lane & 15)] & 0xffffu) + 16u * (lane >> 4), r);
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint32_t pos = es[kk] >> 16;
+#pragma unroll
+              for (int qg = 0; qg < 2; ++qg) {
+                bb1[qg] |= uint32_t(kb1g[qg][pos]) << (8 * kk);
+                bb2[qg] |= uint32_t(kb2g[qg][pos]) << (8 * kk);
+              }
+            }
+            if (ones_col) bb2[0] = bb2[1] = 0x01010101u;
+            const uint32_t x0 = r[2 * half], x1 = r[2 * half + 1];
+#pragma unroll
+            for (int qg = 0; qg < 2; ++qg) {
+              mma_k16(a1[qg][0], high_code<0>(x0), high_code<0>(x1), bb1[qg]);
+              mma_k16(a2[qg][0], high_code<0>(x0), high_code<0>(x1), bb2[qg]);
+              mma_k16(a1[qg][1], high_code<1>(x0), high_code<1>(x1), bb1[qg]);
+              mma_k16(a2[qg][1], high_code<1>(x0), high_code<1>(x1), bb2[qg]);
+              mma_k16(a1[qg][2], high_code<2>(x0), high_code<2>(x1), bb1[qg]);
+              mma_k16(a2[qg][2], high_code<2>(x0), high_code<2>(x1), bb2[qg]);
+              mma_k16(a1[qg][3], high_code<3>(x0), high_code<3>(x1), bb1[qg]);
+              mma_k16(a2[qg][3], high_code<3>(x0), high_code<3>(x1), bb2[qg]);
+            }
+          }
+#pragma unroll
+          for (int qg = 0; qg < 2; ++qg)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+              const float f = cqg[qg] * (i == 0 ? 1.0f : i == 1 ? 0.25f : 0.0625f);
+              const float2 fl = make_float2(f, f), fh = make_float2(f * 65536.0f, f * 65536.0f);
+              const int lo0 = 256 * a1[qg][i][0] + a1[qg][i][1], lo1 = 256 * a1[qg][i][2] + a1[qg][i][3];
+              const int hi0 = a2[qg][i][0] - 64 * a2[qg][i][1], hi1 = a2[qg][i][2] - 64 * a2[qg][i][3];
+              const float2 t = fma2(make_float2(float(lo0), float(lo1)), fl, make_float2(-zqg[qg], -zqg[qg]));
+              const float2 rr = fma2(make_float2(float(hi0), float(hi1)), fh, t);
+              s[qg][8 * half + i] = rr.x;
+              s[qg][8 * half + 4 + i] = rr.y;
+            }
+        }
+      }
+      __syncwarp();
+      // keys consumed: request the next page's keys
+      have_next = cursor_step(cur, a) && cursor_to_page(cur, a, f1);
+      if (lane == 0 && have_next) issue_k(cur);
 
       if (!mbar_wait(bar_v, v_phase)) { failed = true; break; }
       v_phase ^= 1u;
       if (valid) {
-        softmax_step(st, s);   // s -> p
         // ---- P' = p * scale_v as 16-bit fixed point, tokens 32 k + 4 g_ + i (v = 4 k + i)
         uint32_t sz[16];
 #pragma unroll
@@ -670,13 +772,17 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           const uint4 x = *reinterpret_cast<const uint4*>(vbuf + 4096 + 4 * (32 * k + 4 * g_));
           sz[4 * k] = x.x; sz[4 * k + 1] = x.y; sz[4 * k + 2] = x.z; sz[4 * k + 3] = x.w;
         }
+        float dvg[kQG];
+#pragma unroll
+        for (int qg = 0; qg < kQG; ++qg) {
+        softmax_step(st[qg], s[qg]);   // s -> p
         float pp[16];
         float mp = 0.f;
 #pragma unroll
         for (int v = 0; v < 16; v += 2) {
           // (scale, zero) of tokens v and v + 1 -> (scale_v, scale_v+1)
           const float2 sc = T::to_f2(prmt(sz[v], sz[v + 1], 0x5410u));
-          const float2 pr = mul2(make_float2(s[v], s[v + 1]), sc);
+          const float2 pr = mul2(make_float2(s[qg][v], s[qg][v + 1]), sc);
           pp[v] = pr.x;
           pp[v + 1] = pr.y;
           mp = fmaxf(mp, fmaxf(pr.x, pr.y));
@@ -686,6 +792,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
         const float Rv = mp > 0.f ? __fdividef(kValRange, mp) : 0.f;
         const float dv = mp * (1.0f / kValRange);
+        dvg[qg] = dv;
         uint32_t yb[16];
         float2 zv2 = make_float2(0.f, 0.f);
 #pragma unroll
@@ -698,8 +805,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           zv2 = fma2(T::to_f2(zz), y, zv2);
         }
         const float zv = zv2.x + zv2.y;
-        st.zs = __fmaf_rn(zv, dv, st.zs);
-        uint8_t* prow = ptab + q_ * kRow + 4 * g_;
+        st[qg].zs = __fmaf_rn(zv, dv, st[qg].zs);
+        uint8_t* prow = ptab + (q_ + 4 * qg) * kRow + 4 * g_;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           uint32_t y0, y1;
@@ -707,7 +814,11 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           *reinterpret_cast<uint32_t*>(prow + 32 * k) = y0;
           *reinterpret_cast<uint32_t*>(prow + kPlane + 32 * k) = y1;
         }
+        }
         __syncwarp();
+        if constexpr (kQG == 1) {
+        const float dv = dvg[0];
+        State& sto = st[0];
         // ---- values: M = channels, K = tokens 32 ks + k
         int acc[8][4];
         val_kstep<true>(acc, v_row, vb, 0, q_);
@@ -721,9 +832,47 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           const float f = dv * (i == 0 ? 1.0f : i == 1 ? 0.25f : i == 2 ? 0.0625f : 0.015625f);
           const int c0 = 256 * acc[mt][0] + acc[mt][1], c1 = 256 * acc[mt][2] + acc[mt][3];
           const float2 o = fma2(make_float2(float(c0), float(c1)), make_float2(f, f),
-                                make_float2(st.o[8 * half + i], st.o[8 * half + 4 + i]));
-          st.o[8 * half + i] = o.x;
-          st.o[8 * half + 4 + i] = o.y;
+                                make_float2(sto.o[8 * half + i], sto.o[8 * half + 4 + i]));
+          sto.o[8 * half + i] = o.x;
+          sto.o[8 * half + 4 + i] = o.y;
+        }
+        } else {
+          const uint8_t* vbg[2] = {vb, vb + 4 * kRow};
+#pragma unroll
+          for (int half = 0; half < 2; ++half) {
+            int acc[2][4][4];
+#pragma unroll
+            for (int ks = 0; ks < 4; ++ks) {
+              uint32_t bv[2][2];
+#pragma unroll
+              for (int qg = 0; qg < 2; ++qg) {
+                bv[qg][0] = lds32(vbg[qg] + 32 * ks + 4 * q_);
+                bv[qg][1] = lds32(vbg[qg] + 32 * ks + 16 + 4 * q_);
+              }
+              uint32_t r[4];
+              ldsm_t_x2(v_row + 1024u * ks + 16u * half, r);
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const uint32_t m = 0x03030303u << (2 * i);
+#pragma unroll
+                for (int qg = 0; qg < 2; ++qg) {
+                  if (ks == 0) mma_k32_z(acc[qg][i], r[0] & m, r[1] & m, r[2] & m, r[3] & m, bv[qg][0], bv[qg][1]);
+                  else mma_k32(acc[qg][i], r[0] & m, r[1] & m, r[2] & m, r[3] & m, bv[qg][0], bv[qg][1]);
+                }
+              }
+            }
+#pragma unroll
+            for (int qg = 0; qg < 2; ++qg)
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                const float f = dvg[qg] * (i == 0 ? 1.0f : i == 1 ? 0.25f : i == 2 ? 0.0625f : 0.015625f);
+                const int c0 = 256 * acc[qg][i][0] + acc[qg][i][1], c1 = 256 * acc[qg][i][2] + acc[qg][i][3];
+                const float2 o = fma2(make_float2(float(c0), float(c1)), make_float2(f, f),
+                                      make_float2(st[qg].o[8 * half + i], st[qg].o[8 * half + 4 + i]));
+                st[qg].o[8 * half + i] = o.x;
+                st[qg].o[8 * half + 4 + i] = o.y;
+              }
+          }
         }
       }
       __syncwarp();
@@ -734,35 +883,40 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     // ---- advance; write the partial at a segment end or at the end of the slice
     const bool seg_end = pos.p + 1 >= pos.items;
     if (seg_end || f + 1 == f1) {
-      float l = st.l, zs = st.zs;
-      l += __shfl_xor_sync(0xffffffffu, l, 4);
-      l += __shfl_xor_sync(0xffffffffu, l, 8);
-      l += __shfl_xor_sync(0xffffffffu, l, 16);
-      zs += __shfl_xor_sync(0xffffffffu, zs, 4);
-      zs += __shfl_xor_sync(0xffffffffu, zs, 8);
-      zs += __shfl_xor_sync(0xffffffffu, zs, 16);
       const int64_t base = ((int64_t(b) * H + h) * plan.num_splits + slot) * g;
-      if (q_ < g) {
-        // st.o[4 k + i] <-> channel 32 k + 4 g_ + i
-        float* o = plan.ws_o + (base + q_) * kD + 4 * g_;
 #pragma unroll
-        for (int k = 0; k < 4; ++k)
-          *reinterpret_cast<float4*>(o + 32 * k) =
-              make_float4(st.o[4 * k] - zs, st.o[4 * k + 1] - zs, st.o[4 * k + 2] - zs, st.o[4 * k + 3] - zs);
-        if (g_ == 0) {
-          plan.ws_m[base + q_] = st.m == -INFINITY ? -INFINITY : st.m * kLn2;
-          plan.ws_l[base + q_] = l;
+      for (int qg = 0; qg < kQG; ++qg) {
+        State& sq = st[qg];
+        float l = sq.l, zs = sq.zs;
+        l += __shfl_xor_sync(0xffffffffu, l, 4);
+        l += __shfl_xor_sync(0xffffffffu, l, 8);
+        l += __shfl_xor_sync(0xffffffffu, l, 16);
+        zs += __shfl_xor_sync(0xffffffffu, zs, 4);
+        zs += __shfl_xor_sync(0xffffffffu, zs, 8);
+        zs += __shfl_xor_sync(0xffffffffu, zs, 16);
+        const int qh = q_ + 4 * qg;
+        if (qh < g) {
+          // o[4 k + i] <-> channel 32 k + 4 g_ + i
+          float* o = plan.ws_o + (base + qh) * kD + 4 * g_;
+#pragma unroll
+          for (int k = 0; k < 4; ++k)
+            *reinterpret_cast<float4*>(o + 32 * k) =
+                make_float4(sq.o[4 * k] - zs, sq.o[4 * k + 1] - zs, sq.o[4 * k + 2] - zs, sq.o[4 * k + 3] - zs);
+          if (g_ == 0) {
+            plan.ws_m[base + qh] = sq.m == -INFINITY ? -INFINITY : sq.m * kLn2;
+            plan.ws_l[base + qh] = l;
+          }
         }
+        reset_state(sq);
       }
       if (seg_end && lane == 0) plan.ws_count[int64_t(b) * H + h] = slot + 1;
-      reset_state(st);
     }
     if (f + 1 < f1) {
       cursor_step(pos, a);
       if (seg_end) {
         slot = 0;
         __syncwarp();
-        nb = setup_segment(a, pos.b, pos.h, g, wsm, L, lane, qreg);
+        nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane, qreg);
       }
     }
   }
@@ -781,7 +935,7 @@ bool i8_supports(const KittyDecodeArgs& a) {
   auto region_ok = [](const void* p, int64_t s_seq, int64_t s_head, int64_t s_tok) {
     return p == nullptr || (aligned(p, 16) && s_seq % 8 == 0 && s_head % 8 == 0 && s_tok % 8 == 0);
   };
-  return a.head_dim == kD && a.group == kG && g >= 1 && g <= 4 && a.d_boost <= 128 &&
+  return a.head_dim == kD && a.group == kG && g >= 1 && g <= 8 && a.d_boost <= 128 &&
          aligned(a.q, 16) && a.q_s_seq % 8 == 0 && a.q_s_head % 8 == 0 &&
          region_ok(a.sink_k, a.sk_s_seq, a.sk_s_head, a.sk_s_tok) &&
          region_ok(a.sink_v, a.sv_s_seq, a.sv_s_head, a.sv_s_tok) &&
@@ -794,12 +948,18 @@ bool i8_supports(const KittyDecodeArgs& a) {
 
 int i8_ctas_per_sm() { return kCtasPerSm; }
 
+namespace {
+int i8_groups(const KittyDecodeArgs& a) { return a.num_q_heads / a.num_kv_heads > 4 ? 2 : 1; }
+int i8_ctas(int qg) { return qg == 1 ? kCtasPerSm : kCtasPerSmG8; }
+}  // namespace
+
 // Same slicing rule as the fp16 tensor-core variant (see mma_plan).
 void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   const int items_max = a.max_pages_per_seq + dev::kMaxFp16Items;   // pages + fp16 chunk items
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
-  const int64_t warps = int64_t(sm_count) * kCtasPerSm * kWarps;
+  const int ctas_per_sm = i8_ctas(i8_groups(a));
+  const int64_t warps = int64_t(sm_count) * ctas_per_sm * kWarps;
   const int64_t per_warp = std::max<int64_t>(1, int64_t(a.batch) * a.num_kv_heads * items_max / warps);
   const int auto_target = int(std::max<int64_t>(kSlotsTarget, (items_max + per_warp - 1) / per_warp));
   int target = a.num_splits > 0 ? a.num_splits : auto_target;
@@ -809,31 +969,33 @@ void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   plan->num_splits = (items_max + f_min - 1) / f_min + 1;
   const int64_t total_max = int64_t(a.batch) * a.num_kv_heads * items_max;
   const int64_t warps_needed = (total_max + f_min - 1) / f_min;
-  const int64_t ctas = std::min<int64_t>((warps_needed + kWarps - 1) / kWarps, int64_t(sm_count) * kCtasPerSm);
+  const int64_t ctas = std::min<int64_t>((warps_needed + kWarps - 1) / kWarps, int64_t(sm_count) * ctas_per_sm);
   plan->grid = int(std::max<int64_t>(1, ctas));
 }
 
 namespace {
 // shared-memory attribute and resident CTAs per SM of one instantiation, set up once
 // per shared-memory size
-template <bool kBf16>
+template <bool kBf16, int kQG>
 int prepare_i8(int smem, int* blocks) {
   static int configured_bytes = 0;
   if (configured_bytes < smem) {
-    cudaError_t e = cudaFuncSetAttribute(decode_i8_kernel<kBf16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    cudaError_t e =
+        cudaFuncSetAttribute(decode_i8_kernel<kBf16, kQG>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return fail(KITTY_ERR_CUDA, std::string("decode_i8 smem attribute: ") + cudaGetErrorString(e));
     configured_bytes = smem;
   }
   // persistent grid: no more CTAs than fit on the GPU at once (shared memory grows with d_boost)
-  static int occ_smem = -1, occ_blocks = kCtasPerSm;
+  static int occ_smem = -1, occ_blocks = i8_ctas(kQG);
   if (occ_smem != smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16>, kThreads, smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16, kQG>, kThreads, smem) !=
+            cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
       n = 1;
     }
-    occ_blocks = std::min(n, kCtasPerSm);
+    occ_blocks = std::min(n, i8_ctas(kQG));
     occ_smem = smem;
   }
   *blocks = occ_blocks;
@@ -842,11 +1004,13 @@ int prepare_i8(int smem, int* blocks) {
 }  // namespace
 
 int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
-  const Layout L = i8_layout(a.d_boost);
+  const int qg = i8_groups(a);
+  const Layout L = i8_layout(a.d_boost, qg);
   const int smem = kWarps * L.size;
   const bool bf16 = a.dtype == KITTY_DTYPE_BF16;
   int occ_blocks = 1;
-  const int rc = bf16 ? prepare_i8<true>(smem, &occ_blocks) : prepare_i8<false>(smem, &occ_blocks);
+  const int rc = qg == 1 ? (bf16 ? prepare_i8<true, 1>(smem, &occ_blocks) : prepare_i8<false, 1>(smem, &occ_blocks))
+                         : (bf16 ? prepare_i8<true, 2>(smem, &occ_blocks) : prepare_i8<false, 2>(smem, &occ_blocks));
   if (rc != KITTY_OK) return rc;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
@@ -854,8 +1018,13 @@ int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStrea
     sms = 148;
   }
   const int grid = std::max(1, std::min(plan.grid, sms * occ_blocks));
-  if (bf16) decode_i8_kernel<true><<<grid, kThreads, smem, stream>>>(a, plan);
-  else decode_i8_kernel<false><<<grid, kThreads, smem, stream>>>(a, plan);
+  if (qg == 1) {
+    if (bf16) decode_i8_kernel<true, 1><<<grid, kThreads, smem, stream>>>(a, plan);
+    else decode_i8_kernel<false, 1><<<grid, kThreads, smem, stream>>>(a, plan);
+  } else {
+    if (bf16) decode_i8_kernel<true, 2><<<grid, kThreads, smem, stream>>>(a, plan);
+    else decode_i8_kernel<false, 2><<<grid, kThreads, smem, stream>>>(a, plan);
+  }
   return check_launch("decode_i8_kernel");
 }
 

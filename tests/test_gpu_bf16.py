@@ -154,7 +154,7 @@ def test_decode_vs_reference(golden_npz, golden_manifest, name, splits, variant)
                                atol=ATOL, rtol=RTOL)
 
 
-@pytest.mark.parametrize("Hq", [8, 32])
+@pytest.mark.parametrize("Hq", [8, 32, 48, 64])
 def test_random_d128_batches_vs_oracle(Hq, variant):
     """Longer contexts with the benchmark distribution (bf16): kernels vs the oracle."""
     case = synthetic.make_decode_case(77, 3, Hq, 8, 128, [32 + 9 * 128 + 50, 32 + 3 * 128, 20], sink=32, group=128,

@@ -133,6 +133,8 @@ def variant(request):
     (102, 3, 64, 8, [32 + 9 * 128 + 96, 32 + 21 * 128 + 5, 32 + 2 * 128 + 127], 0.125),   # GQA 8:1
     (103, 2, 8, 8, [32 + 6 * 128 + 3, 32 + 11 * 128 + 64], 0.25),                            # MHA, K=32
     (104, 2, 16, 2, [32 + 64 * 128 + 10, 40], 0.25),
+    (105, 3, 48, 8, [32 + 5 * 128 + 17, 32 + 12 * 128, 90], 0.125),                        # 6 q heads per KV head
+    (106, 2, 40, 8, [32 + 7 * 128 + 100, 32 + 128 + 1], 0.25),                             # 5 q heads per KV head
 ])
 def test_random_batches_vs_oracle(seed, B, Hq, H, ctx, rate, variant):
     case = synthetic.make_decode_case(seed, B, Hq, H, 128, ctx, boost_rate=rate)
