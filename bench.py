@@ -51,11 +51,27 @@ sys.path.insert(0, str(ROOT / "kitty-kv_b200"))
 METRIC = "quantized paged decode-attn HBM GB/s (% of peak) & tokens/s at 1/2/4/8 B200"
 # DRAM bytes (read + write) of one decode launch, from one ncu capture
 # (dram__bytes_read.sum + dram__bytes_write.sum) of this script on the same workload
-# and kernel; None where no capture exists.
+# and kernel; None where no capture exists.  Config 4 was captured at batch 8
+# (`--batch 8`, 1/8 of the page-heads) and scaled by 8: its traffic is per page-head.
 MEASURED_TRAFFIC = {
-    ("config2", "decode_i8_kernel"): 652_401_408 + 5_087_744,
+    ("config2", "decode_i8_kernel"): 652_330_752 + 4_749_312,
     ("config2", "decode_mma_kernel"): 652_734_720 + 5_091_328,
+    ("config4", "decode_i8_kernel"): (641_469_184 + 4_378_880) * 8,
 }
+
+def measured_traffic(workload, kernel, world):
+    """Captured DRAM bytes of one decode launch on this rank: the single-GPU capture,
+    divided among the ranks for the workloads whose ranks split one job's page-heads
+    evenly (config 4's KV heads); None where the split is uneven or no capture exists."""
+    t = MEASURED_TRAFFIC.get((workload, kernel))
+    if t is None or world == 1:
+        return t
+    if WORKLOADS[workload].get("shard") == "replica":
+        return t
+    if WORKLOADS[workload].get("shard") == "kv_head":
+        return t // world
+    return None
+
 
 WORKLOADS = {
     "config1": dict(kind="decode", batch=1, num_q_heads=32, num_kv_heads=8, head_dim=128, context=4096,
@@ -635,7 +651,7 @@ def decode_arm(args, spec, d, device, local):
         "e2e": {"value": round(nbytes_total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": MEASURED_TRAFFIC.get((args.workload, kernel)),
+                     "frac": round(achieved / peak, 4), "traffic": measured_traffic(args.workload, kernel, world),
                      "peak_source": f"{peak_kind} copy bandwidth", "kernel": f"{kernel} (+ split merge)",
                      "algorithmic_bytes_per_launch": nbytes_local},
         "cpu_baseline": cpu,
@@ -759,9 +775,16 @@ def main():
     ap.add_argument("--variant", choices=["auto", "simt", "mma", "int8"], default="auto",
                     help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128 "
                          "and up to 8 query heads per KV head, CUDA-core kernel otherwise)")
+    ap.add_argument("--batch", type=int, default=0,
+                    help="override the workload's batch (smaller cases for profiler captures); the JSON "
+                         "line's config then records the reduced batch")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
-    spec = WORKLOADS[args.workload]
+    spec = dict(WORKLOADS[args.workload])
+    if args.batch > 0:
+        if spec["kind"] != "decode" or "batch" not in spec:
+            raise SystemExit("--batch applies to the decode workloads with a fixed batch")
+        spec["batch"] = args.batch
     if args.impl == "reference":
         reference_arm(args, spec)
     else:
