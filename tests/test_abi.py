@@ -55,3 +55,52 @@ def test_null_args_are_rejected_without_a_gpu():
     a.batch, a.num_q_heads, a.num_kv_heads, a.head_dim, a.group = 1, 3, 2, 16, 8
     assert lib.kitty_paged_decode(a, None) == 1          # 3 q heads over 2 kv heads
     assert b"multiple" in lib.kitty_last_error()
+
+
+C_PROGRAM = r"""
+#include <stdio.h>
+#include <string.h>
+#include "kitty_b200.h"
+/* every declared entry point is referenced, so the link checks the exports; only the
+   calls that need no GPU are made */
+typedef int (*any_fn)(void);
+int main(void) {
+  any_fn fns[] = {
+    (any_fn)kitty_quantize_key_pages, (any_fn)kitty_quantize_value_pages, (any_fn)kitty_dequantize_key_pages,
+    (any_fn)kitty_paged_decode_workspace_size, (any_fn)kitty_paged_decode, (any_fn)kitty_paged_decode_noalloc,
+    (any_fn)kitty_device_error_flags, (any_fn)kitty_decode_force_variant, (any_fn)kitty_cache_reset,
+    (any_fn)kitty_cache_append, (any_fn)kitty_cache_prefill, (any_fn)kitty_cache_release};
+  if (kitty_abi_version() != KITTY_ABI_VERSION) return 1;
+  if (kitty_args_size(0) != sizeof(KittyKeyQuantArgs) || kitty_args_size(1) != sizeof(KittyValueQuantArgs) ||
+      kitty_args_size(2) != sizeof(KittyKeyDequantArgs) || kitty_args_size(3) != sizeof(KittyDecodeArgs) ||
+      kitty_args_size(4) != sizeof(KittyCacheState) || kitty_args_size(5) != sizeof(KittyPrefillArgs))
+    return 2;
+  KittyDecodeArgs a;
+  memset(&a, 0, sizeof(a));
+  a.batch = 1; a.num_q_heads = 3; a.num_kv_heads = 2; a.head_dim = 16; a.group = 8;
+  if (kitty_paged_decode(&a, NULL) != KITTY_ERR_INVALID_ARGUMENT) return 3;
+  if (strlen(kitty_last_error()) == 0) return 4;
+  if (kitty_cache_append(NULL, 0, NULL, NULL, 0, 0, NULL, 0, 0, NULL) != KITTY_ERR_INVALID_ARGUMENT) return 5;
+  printf("%d entry points\n", (int)(sizeof(fns) / sizeof(fns[0])));
+  return 0;
+}
+"""
+
+
+def test_header_compiles_as_c_and_links(tmp_path):
+    """A plain C program (gcc, C99) includes the header, references every entry point,
+    links against the library and checks the struct sizes against it (no GPU call)."""
+    import shutil
+    if shutil.which("gcc") is None:
+        pytest.skip("gcc not available")
+    src = tmp_path / "abi_check.c"
+    src.write_text(C_PROGRAM)
+    exe = tmp_path / "abi_check"
+    lib = _lib.library_path()
+    cmd = ["gcc", "-std=c99", "-Wall", "-Werror", "-Wno-cast-function-type", "-I", str(HEADER.parent), str(src),
+           "-o", str(exe), str(lib), f"-Wl,-rpath,{lib.parent}"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    out = subprocess.run([str(exe)], capture_output=True, text=True)
+    assert out.returncode == 0, (out.returncode, out.stdout, out.stderr)
+    assert out.stdout.strip() == f"{len(declared_functions()) - 3} entry points"
