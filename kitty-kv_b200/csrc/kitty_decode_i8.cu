@@ -69,6 +69,9 @@ constexpr int kD = 128, kG = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 constexpr int kSlotsTarget = 16;
+// cost units of one fp16 chunk item in the warps' slicing of the walk (a page is one
+// unit); chunk items cost a warp a few pages' time
+constexpr int kFp16Weight = 2;
 constexpr float kKeyRange = 4194300.0f;     // 2^22 - 4: |x| < 2^22 even with an approximate reciprocal
 constexpr float kValRange = 65535.0f;
 constexpr float kMagicKey = 12582912.0f;    // 1.5 * 2^23: fma(w, R, magic) has bits 0x4B400000 + rint(w R)
@@ -458,13 +461,38 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
   }
 }
 
+// The rows a segment starts with (its q rows, boost-index row and fp16 sink / tail
+// rows) into L2 while the previous segment's last page is processed: the segment
+// setup and the fp16 chunk items that follow then read L2 instead of HBM.
+__device__ __noinline__ void prefetch_segment(const KittyDecodeArgs& a, int b, int cr, int h, int g, int lane) {
+  if (lane < 2 * g)
+    prefetch_l2(reinterpret_cast<const uint8_t*>(a.q) + 2 * (b * a.q_s_seq + int64_t(h * g + (lane >> 1)) * a.q_s_head) +
+                128 * (lane & 1));
+  if (lane == 31) prefetch_l2(a.boost_idx + h * a.bidx_s_head);
+  const int sl = a.sink_len ? a.sink_len[cr] : a.sink_len_all;
+  const int tl = a.tail_len ? a.tail_len[cr] : a.tail_len_all;
+  const uint8_t* sk = reinterpret_cast<const uint8_t*>(a.sink_k) + 2 * (cr * a.sk_s_seq + h * a.sk_s_head);
+  const uint8_t* sv = reinterpret_cast<const uint8_t*>(a.sink_v) + 2 * (cr * a.sv_s_seq + h * a.sv_s_head);
+  const uint8_t* tk = reinterpret_cast<const uint8_t*>(a.tail_k) + 2 * (cr * a.tk_s_seq + h * a.tk_s_head);
+  const uint8_t* tv = reinterpret_cast<const uint8_t*>(a.tail_v) + 2 * (cr * a.tv_s_seq + h * a.tv_s_head);
+  // two 128-byte lines per 128-channel fp16 row
+  for (int i = lane; i < 2 * sl; i += 32) {
+    prefetch_l2(sk + 2 * (i >> 1) * a.sk_s_tok + 128 * (i & 1));
+    prefetch_l2(sv + 2 * (i >> 1) * a.sv_s_tok + 128 * (i & 1));
+  }
+  for (int i = lane; i < 2 * tl; i += 32) {
+    prefetch_l2(tk + 2 * (i >> 1) * a.tk_s_tok + 128 * (i & 1));
+    prefetch_l2(tv + 2 * (i >> 1) * a.tv_s_tok + 128 * (i & 1));
+  }
+}
+
 // kQG groups of four query heads per KV head share each page-head's unpacked
 // operands: with kQG = 2 the key contraction runs one 64-token half at a time
 // (four accumulator sets: two groups x (byte 1, byte 0 | byte 2, code sum)) and the
 // value contraction one 64-channel half at a time.
 template <bool kBf16, int kQG>
 __global__ void __launch_bounds__(kThreads, kQG == 1 ? kCtasPerSm : kCtasPerSmG8)
-decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
+decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constant__ DecodePlan plan) {
   using T = Half16<kBf16>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.d_boost, H = a.num_kv_heads, B = a.batch;
@@ -485,16 +513,31 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // ---- this warp's slice of the item space
   const int64_t gw = int64_t(blockIdx.x) * kWarps + warp;
   const int64_t n_warps = int64_t(gridDim.x) * kWarps;
-  SegmentScan sc = scan_segments(a, B, H, 0, lane);
+  // (units: pages count 1, fp16 chunk items kFp16Weight)
+  SegmentScan sc = scan_segments(a, B, H, 0, lane, kFp16Weight);
   const int64_t total = sc.total;
   int64_t F = (total + n_warps - 1) / n_warps;
   if (F < plan.pages_per_split) F = plan.pages_per_split;
   const int64_t f0 = gw * F;
   if (f0 >= total) return;
   const int64_t f1 = min(total, f0 + F);
-  sc = scan_segments(a, B, H, f0, lane);
-  Cursor pos = make_cursor(a, f0, sc.b, sc.h, sc.p);   // the item being processed
-  int slot = int(gw - sc.seg_begin / F);
+  sc = scan_segments(a, B, H, f0, lane, kFp16Weight);
+  Cursor pos;   // the item being processed: the first one starting in [f0, f1)
+  if (!make_cursor(pos, a, sc.seg_begin, sc.b, sc.h, sc.u, kFp16Weight) || pos.f >= f1) {
+    // No item starts in the slice: it lies inside the span of an fp16 chunk item that
+    // an earlier warp processes.  Its slot of that segment gets a neutral partial (the
+    // merge reads every slot below the segment's count).
+    const int64_t base = ((int64_t(sc.b) * H + sc.h) * plan.num_splits + int(gw - sc.seg_begin / F)) * g;
+    for (int i = lane; i < g; i += 32) {
+      plan.ws_m[base + i] = -INFINITY;
+      plan.ws_l[base + i] = 0.f;
+    }
+    for (int i = lane; i < g * kD; i += 32) plan.ws_o[base * kD + i] = 0.f;
+    return;
+  }
+  const int64_t pos_unit = pos.p <= pos.n16 ? int64_t(kFp16Weight) * pos.p
+                                            : int64_t(kFp16Weight) * pos.n16 + (pos.p - pos.n16);
+  int slot = int(gw - (pos.f - pos_unit) / F);
 
   if (lane == 0) {
     mbar_init(bar_k, 1);
@@ -512,10 +555,22 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   uint32_t k_phase = 0, v_phase = 0;
   bool failed = false;
 
-  // physical page of page item p (>= n16) of sequence bb
-  auto phys = [&](int bb, int pp, int n16) -> int64_t { return a.block_table[bb * a.bt_s_seq + (pp - n16)]; };
-  auto issue_k = [&](const Cursor& c) {
-    int64_t page = phys(c.s, c.p, c.n16);
+  // Block-table window: lane l holds the physical page of page index bt_base + l of
+  // cache row bt_row, so the page of the next copy is a register shuffle instead of a
+  // dependent global load on the copy-issue path (reloaded once per 32 pages or at a
+  // segment change).  Warp-uniform.
+  int bt_row = -1, bt_base = 0, bt_val = 0;
+  auto page_of = [&](const Cursor& c) -> int64_t {
+    const int idx = c.p - c.n16;
+    if (c.s != bt_row || idx < bt_base || idx >= bt_base + 32) {
+      bt_row = c.s;
+      bt_base = idx;
+      const int e = idx + lane;
+      bt_val = e < c.items - c.n16 ? a.block_table[int64_t(c.s) * a.bt_s_seq + e] : -1;
+    }
+    return __shfl_sync(0xffffffffu, bt_val, idx - bt_base);
+  };
+  auto issue_k = [&](const Cursor& c, int64_t page) {
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_k, k_tx);
@@ -523,8 +578,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     bulk_g2s(smem_u32(kbuf + 4096), reinterpret_cast<const uint8_t*>(a.key_meta) + phh * (2 * kD * 2), 512u, bar_k);
     if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
   };
-  auto issue_v = [&](const Cursor& c) {
-    int64_t page = phys(c.s, c.p, c.n16);
+  auto issue_v = [&](const Cursor& c, int64_t page) {
     if (page < 0 || page >= a.pool_pages) page = 0;
     const int64_t phh = page * H + c.h;
     mbar_arrive_expect_tx(bar_v, v_tx);
@@ -533,9 +587,25 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   };
 
   Cursor cur = pos;
-  bool have_next = cursor_to_page(cur, a, f1);
-  if (lane == 0 && have_next) { issue_k(cur); issue_v(cur); }
+  bool have_next = cursor_to_page(cur, a, f1, kFp16Weight);
+  int64_t cur_page = have_next ? page_of(cur) : -1;   // physical page of cur (the copies in flight)
+  if (lane == 0 && have_next) { issue_k(cur, cur_page); issue_v(cur, cur_page); }
   __syncwarp();
+  // the key (value) buffer has been read by every lane: request the next page's keys
+  // (values) at once, before the epilogue that only needs registers
+  bool seg_ahead = false;   // cur has entered a new segment: prefetch its rows after this page
+  auto next_keys = [&]() {
+    __syncwarp();
+    const int ob = cur.b, oh = cur.h;
+    have_next = cursor_step(cur, a, kFp16Weight) && cursor_to_page(cur, a, f1, kFp16Weight);
+    cur_page = have_next ? page_of(cur) : -1;
+    if (lane == 0 && have_next) issue_k(cur, cur_page);
+    seg_ahead = have_next && (cur.b != ob || cur.h != oh);
+  };
+  auto next_values = [&]() {
+    __syncwarp();
+    if (lane == 0 && have_next) issue_v(cur, cur_page);
+  };
 
   State st[kQG];
 #pragma unroll
@@ -551,7 +621,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   const bool ones_col = (g_ & 1) != 0;                                          // odd columns: all-ones plane
   const uint8_t* vb = ptab + ((g_ & 1) ? 0 : 1) * kPlane + (g_ >> 1) * kRow;    // y1 | y0
 
-  for (int64_t f = f0; f < f1; ++f) {
+  for (;;) {   // the items starting in [f0, f1)
     const int b = pos.b, h = pos.h;
     if (pos.p < pos.n16) {
       int t0, t1;
@@ -560,8 +630,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       for (int qg = 0; qg < kQG; ++qg)
         process_fp16_region<kBf16>(a, b, h, g, 4 * qg, st[qg], wsm, L, qk_scale, lane, t0, t1);
     } else {
-      const int64_t page = phys(pos.s, pos.p, pos.n16);
-      const bool valid = page >= 0 && page < a.pool_pages;
+      const bool valid = cur_page >= 0 && cur_page < a.pool_pages;   // cur is this page
       if (!mbar_wait(bar_k, k_phase)) { failed = true; break; }
       k_phase ^= 1u;
       const uint8_t* km = kbuf + 4096;   // scale[128] fp16, zero[128] fp16
@@ -662,6 +731,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           mma_k16(acc2[4 * half + 3], high_code<3>(x0), high_code<3>(x1), bb2);
         }
       }
+      next_keys();
       {
         // row factors 1, 4, 16, 16 of code i
 #pragma unroll
@@ -757,13 +827,11 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
             }
         }
       }
-      __syncwarp();
-      // keys consumed: request the next page's keys
-      have_next = cursor_step(cur, a) && cursor_to_page(cur, a, f1);
-      if (lane == 0 && have_next) issue_k(cur);
+      if constexpr (kQG != 1) next_keys();
 
       if (!mbar_wait(bar_v, v_phase)) { failed = true; break; }
       v_phase ^= 1u;
+      bool v_requested = false;
       if (valid) {
         // ---- P' = p * scale_v as 16-bit fixed point, tokens 32 k + 4 g_ + i (v = 4 k + i)
         uint32_t sz[16];
@@ -824,6 +892,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         val_kstep<true>(acc, v_row, vb, 0, q_);
 #pragma unroll
         for (int ks = 1; ks < 4; ++ks) val_kstep<false>(acc, v_row + 1024u * ks, vb, ks, q_);
+        next_values();
+        v_requested = true;
         // ---- accumulate: tile 4 half + i holds channels 64 half + 4 g_ + i (row g_) and
         // + 32 (row g_ + 8), i.e. st.o[8 half + i] and st.o[8 half + 4 + i]; row factor 4^i
 #pragma unroll
@@ -875,14 +945,17 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           }
         }
       }
-      __syncwarp();
-      // values consumed: request the next page's values
-      if (lane == 0 && have_next) issue_v(cur);
+      if (!v_requested) next_values();
+      if (seg_ahead) {   // here, where few registers are live
+        prefetch_segment(a, cur.b, cur.s, cur.h, g, lane);
+        seg_ahead = false;
+      }
     }
 
     // ---- advance; write the partial at a segment end or at the end of the slice
     const bool seg_end = pos.p + 1 >= pos.items;
-    if (seg_end || f + 1 == f1) {
+    const bool last = pos.f + cursor_width(pos, kFp16Weight) >= f1;   // no item of the slice follows
+    if (seg_end || last) {
       const int64_t base = ((int64_t(b) * H + h) * plan.num_splits + slot) * g;
 #pragma unroll
       for (int qg = 0; qg < kQG; ++qg) {
@@ -911,13 +984,12 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       }
       if (seg_end && lane == 0) plan.ws_count[int64_t(b) * H + h] = slot + 1;
     }
-    if (f + 1 < f1) {
-      cursor_step(pos, a);
-      if (seg_end) {
-        slot = 0;
-        __syncwarp();
-        nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane, qreg);
-      }
+    if (last) break;
+    cursor_step(pos, a, kFp16Weight);
+    if (seg_end) {
+      slot = 0;
+      __syncwarp();
+      nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane, qreg);
     }
   }
   if (failed) {
@@ -955,7 +1027,8 @@ int i8_ctas(int qg) { return qg == 1 ? kCtasPerSm : kCtasPerSmG8; }
 
 // Same slicing rule as the fp16 tensor-core variant (see mma_plan).
 void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
-  const int items_max = a.max_pages_per_seq + dev::kMaxFp16Items;   // pages + fp16 chunk items
+  // cost units of the longest segment: pages + weighted fp16 chunk items
+  const int items_max = a.max_pages_per_seq + kFp16Weight * dev::kMaxFp16Items;
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
   const int ctas_per_sm = i8_ctas(i8_groups(a));

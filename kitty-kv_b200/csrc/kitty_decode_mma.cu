@@ -376,7 +376,8 @@ decode_mma_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   if (f0 >= total) return;
   const int64_t f1 = min(total, f0 + F);
   sc = scan_segments(a, B, H, f0, lane);
-  Cursor pos = make_cursor(a, f0, sc.b, sc.h, sc.p);   // the item being processed
+  Cursor pos;   // the item being processed
+  make_cursor(pos, a, sc.seg_begin, sc.b, sc.h, sc.u);
   int slot = int(gw - sc.seg_begin / F);
 
   if (lane == 0) {
