@@ -62,9 +62,15 @@ namespace {
 
 using namespace dev;
 
-constexpr int kWarps = 4;
-constexpr int kThreads = kWarps * 32;
-constexpr int kCtasPerSm = 3;
+// Resident warps per SM: 12 with up to 4 query heads per KV head (<= 170 registers),
+// as one CTA: warps of one CTA share a scheduling age, while with three CTAs of four
+// the oldest CTA's warps won the issue slots and finished well before the youngest,
+// which then set the kernel's end (config 2: 1.5 % slower).  With 8 query heads (255
+// registers) 8 warps per SM, as two CTAs of four (7 % faster than one CTA of eight).
+template <int kQG>
+__host__ __device__ constexpr int warps_per_cta() { return kQG == 1 ? 12 : 4; }
+template <int kQG>
+__host__ __device__ constexpr int ctas_per_sm() { return kQG == 1 ? 1 : 2; }
 constexpr int kD = 128, kG = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -79,12 +85,11 @@ constexpr float kMagicVal = 8388608.0f;     // 2^23: fma(P', Rv, magic) has bits
 constexpr int kRow = 160;                   // digit table: query-head row stride (bytes; 40 words = 8 mod 32)
 // digit table plane stride for 4 (8) query-head rows: 164 (324) words = 4 mod 32 banks
 __host__ __device__ constexpr int plane_bytes(int qg) { return qg == 1 ? 656 : 1296; }
-constexpr int kCtasPerSmG8 = 2;              // resident CTAs per SM of the 8-query-head kernel
 constexpr int kPhRow = 136;                 // fp16 P staging (fp16 region): row stride in halves
 
 // per-warp shared memory (bytes)
 struct Layout {
-  int kbuf, vbuf, dtab, ptab, ent, bars, size, plane;
+  int kbuf, vbuf, dtab, ptab, ent, qs, bars, size, plane;
 };
 // qg = groups of four query heads per KV head (1: g <= 4, 2: g <= 8)
 __host__ __device__ inline Layout i8_layout(int K, int qg) {
@@ -96,6 +101,7 @@ __host__ __device__ inline Layout i8_layout(int K, int qg) {
   L.dtab = o; o += 3 * L.plane;                              // key digits b0, b1, b2 [qh][channel]
   L.ptab = o; o += 2 * L.plane;                              // P' digits y0, y1 [qh][token] / fp16 P (fp16 region)
   L.ent = o;  o += 128 * 4;                                  // boosted entries (row offset | position << 16)
+  L.qs = o;   o += 1024 * qg;                                // q of the prep lanes [qg][half][lane] (16 B each)
   L.bars = o; o += 16;
   L.size = (o + 127) & ~127;
   return L;
@@ -278,24 +284,25 @@ __device__ __forceinline__ void softmax_step(State& st, float (&s)[16]) {
   st.l += sum.x + sum.y;
 }
 
-// Per-segment setup: q of the prep lane's (query heads pq + 4 qg, 16 channels) and the
+// Per-segment setup: q of the prep lane's (query heads pq + 4 qg, 16 channels), kept in
+// shared memory rather than registers (read once per page by the digit step), and the
 // boosted-entry table.  Returns the number of boosted entries.
 template <int kQG>
 __device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint8_t* wsm, const Layout& L,
-                             int lane, uint32_t (&qreg)[kQG][8]) {
+                             int lane) {
   const int pq = lane >> 3, cb = lane & 7;
 #pragma unroll
   for (int qg = 0; qg < kQG; ++qg) {
+    uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
     if (pq + 4 * qg < g) {
       const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
                                                         int64_t(h * g + pq + 4 * qg) * a.q_s_head + 16 * cb);
-      const uint4 x0 = src[0], x1 = src[1];
-      qreg[qg][0] = x0.x; qreg[qg][1] = x0.y; qreg[qg][2] = x0.z; qreg[qg][3] = x0.w;
-      qreg[qg][4] = x1.x; qreg[qg][5] = x1.y; qreg[qg][6] = x1.z; qreg[qg][7] = x1.w;
-    } else {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) qreg[qg][i] = 0u;
+      x0 = src[0];
+      x1 = src[1];
     }
+    uint4* qs = reinterpret_cast<uint4*>(wsm + L.qs + 1024 * qg);
+    qs[lane] = x0;
+    qs[32 + lane] = x1;
   }
   uint32_t* ent = reinterpret_cast<uint32_t*>(wsm + L.ent);
   const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
@@ -461,38 +468,13 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
   }
 }
 
-// The rows a segment starts with (its q rows, boost-index row and fp16 sink / tail
-// rows) into L2 while the previous segment's last page is processed: the segment
-// setup and the fp16 chunk items that follow then read L2 instead of HBM.
-__device__ __noinline__ void prefetch_segment(const KittyDecodeArgs& a, int b, int cr, int h, int g, int lane) {
-  if (lane < 2 * g)
-    prefetch_l2(reinterpret_cast<const uint8_t*>(a.q) + 2 * (b * a.q_s_seq + int64_t(h * g + (lane >> 1)) * a.q_s_head) +
-                128 * (lane & 1));
-  if (lane == 31) prefetch_l2(a.boost_idx + h * a.bidx_s_head);
-  const int sl = a.sink_len ? a.sink_len[cr] : a.sink_len_all;
-  const int tl = a.tail_len ? a.tail_len[cr] : a.tail_len_all;
-  const uint8_t* sk = reinterpret_cast<const uint8_t*>(a.sink_k) + 2 * (cr * a.sk_s_seq + h * a.sk_s_head);
-  const uint8_t* sv = reinterpret_cast<const uint8_t*>(a.sink_v) + 2 * (cr * a.sv_s_seq + h * a.sv_s_head);
-  const uint8_t* tk = reinterpret_cast<const uint8_t*>(a.tail_k) + 2 * (cr * a.tk_s_seq + h * a.tk_s_head);
-  const uint8_t* tv = reinterpret_cast<const uint8_t*>(a.tail_v) + 2 * (cr * a.tv_s_seq + h * a.tv_s_head);
-  // two 128-byte lines per 128-channel fp16 row
-  for (int i = lane; i < 2 * sl; i += 32) {
-    prefetch_l2(sk + 2 * (i >> 1) * a.sk_s_tok + 128 * (i & 1));
-    prefetch_l2(sv + 2 * (i >> 1) * a.sv_s_tok + 128 * (i & 1));
-  }
-  for (int i = lane; i < 2 * tl; i += 32) {
-    prefetch_l2(tk + 2 * (i >> 1) * a.tk_s_tok + 128 * (i & 1));
-    prefetch_l2(tv + 2 * (i >> 1) * a.tv_s_tok + 128 * (i & 1));
-  }
-}
-
 // kQG groups of four query heads per KV head share each page-head's unpacked
 // operands: with kQG = 2 the key contraction runs one 64-token half at a time
 // (four accumulator sets: two groups x (byte 1, byte 0 | byte 2, code sum)) and the
 // value contraction one 64-channel half at a time.
 template <bool kBf16, int kQG>
-__global__ void __launch_bounds__(kThreads, kQG == 1 ? kCtasPerSm : kCtasPerSmG8)
-decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constant__ DecodePlan plan) {
+__global__ void __launch_bounds__(32 * warps_per_cta<kQG>(), ctas_per_sm<kQG>())
+decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   using T = Half16<kBf16>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.d_boost, H = a.num_kv_heads, B = a.batch;
@@ -511,8 +493,9 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
   const uint32_t bar_k = smem_u32(wsm + L.bars), bar_v = bar_k + 8;
 
   // ---- this warp's slice of the item space
-  const int64_t gw = int64_t(blockIdx.x) * kWarps + warp;
-  const int64_t n_warps = int64_t(gridDim.x) * kWarps;
+  // slice index: warp-major over the CTAs, so a small job spreads over many SMs
+  const int64_t gw = int64_t(warp) * gridDim.x + blockIdx.x;
+  const int64_t n_warps = int64_t(gridDim.x) * warps_per_cta<kQG>();
   // (units: pages count 1, fp16 chunk items kFp16Weight)
   SegmentScan sc = scan_segments(a, B, H, 0, lane, kFp16Weight);
   const int64_t total = sc.total;
@@ -560,7 +543,7 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
   // dependent global load on the copy-issue path (reloaded once per 32 pages or at a
   // segment change).  Warp-uniform.
   int bt_row = -1, bt_base = 0, bt_val = 0;
-  auto page_of = [&](const Cursor& c) -> int64_t {
+  auto page_of = [&](const Cursor& c) -> int {
     const int idx = c.p - c.n16;
     if (c.s != bt_row || idx < bt_base || idx >= bt_base + 32) {
       bt_row = c.s;
@@ -570,17 +553,17 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
     }
     return __shfl_sync(0xffffffffu, bt_val, idx - bt_base);
   };
-  auto issue_k = [&](const Cursor& c, int64_t page) {
+  auto issue_k = [&](const Cursor& c, int page) {
     if (page < 0 || page >= a.pool_pages) page = 0;
-    const int64_t phh = page * H + c.h;
+    const int64_t phh = int64_t(page) * H + c.h;
     mbar_arrive_expect_tx(bar_k, k_tx);
     bulk_g2s(smem_u32(kbuf), a.key_low + phh * ph_low, 4096u, bar_k);
     bulk_g2s(smem_u32(kbuf + 4096), reinterpret_cast<const uint8_t*>(a.key_meta) + phh * (2 * kD * 2), 512u, bar_k);
     if (bytes_high) bulk_g2s(smem_u32(kbuf + 4608), a.key_high + phh * ph_high, bytes_high, bar_k);
   };
-  auto issue_v = [&](const Cursor& c, int64_t page) {
+  auto issue_v = [&](const Cursor& c, int page) {
     if (page < 0 || page >= a.pool_pages) page = 0;
-    const int64_t phh = page * H + c.h;
+    const int64_t phh = int64_t(page) * H + c.h;
     mbar_arrive_expect_tx(bar_v, v_tx);
     bulk_g2s(smem_u32(vbuf), a.val_codes + phh * ph_low, 4096u, bar_v);
     bulk_g2s(smem_u32(vbuf + 4096), reinterpret_cast<const uint8_t*>(a.val_meta) + phh * (2 * kG * 2), 512u, bar_v);
@@ -588,19 +571,16 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
 
   Cursor cur = pos;
   bool have_next = cursor_to_page(cur, a, f1, kFp16Weight);
-  int64_t cur_page = have_next ? page_of(cur) : -1;   // physical page of cur (the copies in flight)
+  int cur_page = have_next ? page_of(cur) : -1;   // physical page of cur (the copies in flight)
   if (lane == 0 && have_next) { issue_k(cur, cur_page); issue_v(cur, cur_page); }
   __syncwarp();
   // the key (value) buffer has been read by every lane: request the next page's keys
   // (values) at once, before the epilogue that only needs registers
-  bool seg_ahead = false;   // cur has entered a new segment: prefetch its rows after this page
   auto next_keys = [&]() {
     __syncwarp();
-    const int ob = cur.b, oh = cur.h;
     have_next = cursor_step(cur, a, kFp16Weight) && cursor_to_page(cur, a, f1, kFp16Weight);
     cur_page = have_next ? page_of(cur) : -1;
     if (lane == 0 && have_next) issue_k(cur, cur_page);
-    seg_ahead = have_next && (cur.b != ob || cur.h != oh);
   };
   auto next_values = [&]() {
     __syncwarp();
@@ -610,8 +590,7 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
   State st[kQG];
 #pragma unroll
   for (int qg = 0; qg < kQG; ++qg) reset_state(st[qg]);
-  uint32_t qreg[kQG][8];
-  int nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane, qreg);
+  int nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane);
 
   // ldmatrix row addresses: row `lane` of a 32-row k-step of the key / value plane
   const uint32_t k_row = smem_u32(kbuf) + 32u * lane, v_row = smem_u32(vbuf) + 32u * lane;
@@ -646,12 +625,15 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
       const uint32_t zw[8] = {z0.x, z0.y, z0.z, z0.w, z1.x, z1.y, z1.z, z1.w};
 #pragma unroll
       for (int qg = 0; qg < kQG; ++qg) {
+        const uint4* qs = reinterpret_cast<const uint4*>(wsm + L.qs + 1024 * qg);
+        const uint4 q0 = qs[lane], q1 = qs[32 + lane];
+        const uint32_t qw[8] = {q0.x, q0.y, q0.z, q0.w, q1.x, q1.y, q1.z, q1.w};
         float w[16];
         float mx = 0.f;
 #pragma unroll
         for (int j = 0; j < 8; ++j) {
-          w[2 * j] = mul_h16_f32<kBf16>(uint16_t(qreg[qg][j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
-          w[2 * j + 1] = mul_h16_f32<kBf16>(uint16_t(qreg[qg][j] >> 16), uint16_t(sw[j] >> 16));
+          w[2 * j] = mul_h16_f32<kBf16>(uint16_t(qw[j] & 0xffffu), uint16_t(sw[j] & 0xffffu));
+          w[2 * j + 1] = mul_h16_f32<kBf16>(uint16_t(qw[j] >> 16), uint16_t(sw[j] >> 16));
           mx = fmaxf(mx, fmaxf(fabsf(w[2 * j]), fabsf(w[2 * j + 1])));
         }
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
@@ -946,10 +928,6 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
         }
       }
       if (!v_requested) next_values();
-      if (seg_ahead) {   // here, where few registers are live
-        prefetch_segment(a, cur.b, cur.s, cur.h, g, lane);
-        seg_ahead = false;
-      }
     }
 
     // ---- advance; write the partial at a segment end or at the end of the slice
@@ -989,7 +967,7 @@ decode_i8_kernel(const __grid_constant__ KittyDecodeArgs a, const __grid_constan
     if (seg_end) {
       slot = 0;
       __syncwarp();
-      nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane, qreg);
+      nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane);
     }
   }
   if (failed) {
@@ -1018,11 +996,12 @@ bool i8_supports(const KittyDecodeArgs& a) {
            aligned(a.val_meta, 16) && (a.d_boost == 0 || aligned(a.key_high, 16))));
 }
 
-int i8_ctas_per_sm() { return kCtasPerSm; }
+int i8_ctas_per_sm() { return 1; }
 
 namespace {
 int i8_groups(const KittyDecodeArgs& a) { return a.num_q_heads / a.num_kv_heads > 4 ? 2 : 1; }
-int i8_ctas(int qg) { return qg == 1 ? kCtasPerSm : kCtasPerSmG8; }
+int i8_warps(int qg) { return qg == 1 ? warps_per_cta<1>() : warps_per_cta<2>(); }
+int i8_ctas(int qg) { return qg == 1 ? ctas_per_sm<1>() : ctas_per_sm<2>(); }
 }  // namespace
 
 // Same slicing rule as the fp16 tensor-core variant (see mma_plan).
@@ -1031,8 +1010,8 @@ void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   const int items_max = a.max_pages_per_seq + kFp16Weight * dev::kMaxFp16Items;
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
-  const int ctas_per_sm = i8_ctas(i8_groups(a));
-  const int64_t warps = int64_t(sm_count) * ctas_per_sm * kWarps;
+  const int qg = i8_groups(a);
+  const int64_t warps = int64_t(sm_count) * i8_ctas(qg) * i8_warps(qg);
   const int64_t per_warp = std::max<int64_t>(1, int64_t(a.batch) * a.num_kv_heads * items_max / warps);
   const int auto_target = int(std::max<int64_t>(kSlotsTarget, (items_max + per_warp - 1) / per_warp));
   int target = a.num_splits > 0 ? a.num_splits : auto_target;
@@ -1042,8 +1021,9 @@ void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   plan->num_splits = (items_max + f_min - 1) / f_min + 1;
   const int64_t total_max = int64_t(a.batch) * a.num_kv_heads * items_max;
   const int64_t warps_needed = (total_max + f_min - 1) / f_min;
-  const int64_t ctas = std::min<int64_t>((warps_needed + kWarps - 1) / kWarps, int64_t(sm_count) * ctas_per_sm);
-  plan->grid = int(std::max<int64_t>(1, ctas));
+  // slices are interleaved over the CTAs, so fewer slices than CTA slots need only as
+  // many CTAs as slices
+  plan->grid = int(std::max<int64_t>(1, std::min<int64_t>(warps_needed, int64_t(sm_count) * i8_ctas(qg))));
 }
 
 namespace {
@@ -1059,16 +1039,16 @@ int prepare_i8(int smem, int* blocks) {
     configured_bytes = smem;
   }
   // persistent grid: no more CTAs than fit on the GPU at once (shared memory grows with d_boost)
-  static int occ_smem = -1, occ_blocks = i8_ctas(kQG);
+  static int occ_smem = -1, occ_blocks = 1;
   if (occ_smem != smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16, kQG>, kThreads, smem) !=
-            cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16, kQG>, 32 * warps_per_cta<kQG>(),
+                                                      smem) != cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
       n = 1;
     }
-    occ_blocks = std::min(n, i8_ctas(kQG));
+    occ_blocks = std::min(n, ctas_per_sm<kQG>());
     occ_smem = smem;
   }
   *blocks = occ_blocks;
@@ -1079,7 +1059,8 @@ int prepare_i8(int smem, int* blocks) {
 int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
   const int qg = i8_groups(a);
   const Layout L = i8_layout(a.d_boost, qg);
-  const int smem = kWarps * L.size;
+  const int warps = i8_warps(qg);
+  const int smem = warps * L.size;
   const bool bf16 = a.dtype == KITTY_DTYPE_BF16;
   int occ_blocks = 1;
   const int rc = qg == 1 ? (bf16 ? prepare_i8<true, 1>(smem, &occ_blocks) : prepare_i8<false, 1>(smem, &occ_blocks))
@@ -1092,11 +1073,11 @@ int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStrea
   }
   const int grid = std::max(1, std::min(plan.grid, sms * occ_blocks));
   if (qg == 1) {
-    if (bf16) decode_i8_kernel<true, 1><<<grid, kThreads, smem, stream>>>(a, plan);
-    else decode_i8_kernel<false, 1><<<grid, kThreads, smem, stream>>>(a, plan);
+    if (bf16) decode_i8_kernel<true, 1><<<grid, 32 * warps, smem, stream>>>(a, plan);
+    else decode_i8_kernel<false, 1><<<grid, 32 * warps, smem, stream>>>(a, plan);
   } else {
-    if (bf16) decode_i8_kernel<true, 2><<<grid, kThreads, smem, stream>>>(a, plan);
-    else decode_i8_kernel<false, 2><<<grid, kThreads, smem, stream>>>(a, plan);
+    if (bf16) decode_i8_kernel<true, 2><<<grid, 32 * warps, smem, stream>>>(a, plan);
+    else decode_i8_kernel<false, 2><<<grid, 32 * warps, smem, stream>>>(a, plan);
   }
   return check_launch("decode_i8_kernel");
 }
