@@ -249,10 +249,18 @@ __device__ __forceinline__ void reset_state(State& st) {
 
 // Online-softmax step over the lane's 16 scores (log2 domain; -inf = masked).
 // Returns p in s.
+// three-input maximum (sm_100 form of max.f32)
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+__device__ __forceinline__ float max16(const float (&x)[16], float init) {
+  return fmax3(fmax3(fmax3(x[0], x[1], x[2]), fmax3(x[3], x[4], x[5]), fmax3(x[6], x[7], x[8])),
+               fmax3(x[9], x[10], x[11]), fmax3(fmax3(x[12], x[13], x[14]), x[15], init));
+}
 __device__ __forceinline__ void softmax_step(State& st, float (&s)[16]) {
-  float mx = s[0];
-#pragma unroll
-  for (int v = 1; v < 16; ++v) mx = fmaxf(mx, s[v]);
+  float mx = max16(s, -INFINITY);
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 8));
   mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 16));
@@ -827,7 +835,6 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         for (int qg = 0; qg < kQG; ++qg) {
         softmax_step(st[qg], s[qg]);   // s -> p
         float pp[16];
-        float mp = 0.f;
 #pragma unroll
         for (int v = 0; v < 16; v += 2) {
           // (scale, zero) of tokens v and v + 1 -> (scale_v, scale_v+1)
@@ -835,8 +842,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           const float2 pr = mul2(make_float2(s[qg][v], s[qg][v + 1]), sc);
           pp[v] = pr.x;
           pp[v + 1] = pr.y;
-          mp = fmaxf(mp, fmaxf(pr.x, pr.y));
         }
+        float mp = max16(pp, 0.f);
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 4));
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
