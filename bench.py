@@ -597,18 +597,27 @@ def decode_arm(args, spec, d, device, local):
         ms, _ = timed(stream, args.steps, step, torch, device, d)
     decode_ms, launch_ms = timed(stream, args.steps, run_decode, torch, device, d)
 
-    # ---- end to end through the public API with host buffers
-    q_host = w["q"].cpu().pin_memory()
-    bt_host = w["bt"].cpu().pin_memory()
-    npg_host = w["npg"].cpu().pin_memory()
+    # ---- end to end through the public API with host buffers: a step's inputs (q, block
+    # table, page counts) sit in one pinned staging buffer and cross to the device in one
+    # copy (as a serving loop would stage them); the output comes back in another
+    def pack(ts):
+        parts = [t.cpu().contiguous().view(torch.uint8).reshape(-1) for t in ts]
+        host = torch.empty(sum(p.numel() for p in parts), dtype=torch.uint8).pin_memory()
+        views, at = [], 0
+        for t, p in zip(ts, parts):
+            host[at:at + p.numel()].copy_(p)
+            views.append((at, p.numel(), t.dtype, t.shape))
+            at += p.numel()   # q (fp16) first, then the int32 tables: 4-byte aligned
+        return host, views
+    in_host, in_views = pack([w["q"], w["bt"], w["npg"]])
+    in_dev = torch.empty_like(in_host, device=device)
     out_host = torch.empty(B, Hq, D, dtype=torch.float16).pin_memory()
-    h2d = q_host.numel() * 2 + bt_host.numel() * 4 + npg_host.numel() * 4
+    h2d = in_host.numel()
     d2h = out_host.numel() * 2
 
     def e2e_step():
-        q = q_host.to(device, non_blocking=True)
-        bt = bt_host.to(device, non_blocking=True)
-        npg = npg_host.to(device, non_blocking=True)
+        in_dev.copy_(in_host, non_blocking=True)
+        q, bt, npg = (in_dev[at:at + n].view(dt).view(shape) for at, n, dt, shape in in_views)
         o = decode_call(w, q=q, bt=bt, npg=npg)
         if gather:
             gather_head_outputs(o.permute(1, 0, 2).contiguous())
