@@ -647,7 +647,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
         mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 4));
-        const float R = mx > 0.f ? __fdividef(kKeyRange, mx) : 0.f;
+        const float R = mx > 0.f ? kKeyRange * rcp_approx(mx) : 0.f;   // mx is 0 or >= 2^-48 (fp16 x fp16)
         delta[qg] = mx * (1.0f / kKeyRange);
         uint32_t fb[16];
         float2 zs2 = make_float2(0.f, 0.f);
@@ -847,7 +847,9 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 4));
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 8));
         mp = fmaxf(mp, __shfl_xor_sync(0xffffffffu, mp, 16));
-        const float Rv = mp > 0.f ? __fdividef(kValRange, mp) : 0.f;
+        // a page whose largest weighted probability is below 1e-30 adds nothing next to the
+        // row maximum (weight 1): its digits are left at zero
+        const float Rv = mp > 1e-30f ? kValRange * rcp_approx(mp) : 0.f;
         const float dv = mp * (1.0f / kValRange);
         dvg[qg] = dv;
         uint32_t yb[16];

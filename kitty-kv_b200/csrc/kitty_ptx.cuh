@@ -32,9 +32,17 @@ __device__ __forceinline__ uint32_t pack_f32x2(float lo, float hi) {
   asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(r) : "f"(hi), "f"(lo));
   return r;
 }
+// 2^x for the softmax weights (x <= 0).  The .ftz form is a single instruction; results
+// below 2^-126 become 0, far below anything a weight contributes next to the row maximum.
 __device__ __forceinline__ float ex2(float x) {
   float r;
-  asm("ex2.approx.f32 %0, %1;" : "=f"(r) : "f"(x));
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
+  return r;
+}
+// approximate 1/x (x a normal float), single instruction
+__device__ __forceinline__ float rcp_approx(float x) {
+  float r;
+  asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(r) : "f"(x));
   return r;
 }
 // Packed fp32 pairs (two lanes of work per instruction, IEEE round-to-nearest
