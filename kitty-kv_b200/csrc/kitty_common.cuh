@@ -73,6 +73,9 @@ struct Half16<false> {
     memcpy(&h, &x, 4);
     return __half22float2(h);
   }
+  // low / high 16-bit half of a word as float (one conversion each, no repacking)
+  static __device__ __forceinline__ float lo_f(uint32_t x) { return __half2float(__ushort_as_half(uint16_t(x))); }
+  static __device__ __forceinline__ float hi_f(uint32_t x) { return __half2float(__ushort_as_half(uint16_t(x >> 16))); }
   static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
     __half2 x, y;
     memcpy(&x, &a, 4); memcpy(&y, &b, 4);
@@ -96,6 +99,8 @@ struct Half16<true> {
   static __device__ __forceinline__ float2 to_f2(uint32_t x) {
     return make_float2(__uint_as_float(x << 16), __uint_as_float(x & 0xffff0000u));
   }
+  static __device__ __forceinline__ float lo_f(uint32_t x) { return __uint_as_float(x << 16); }
+  static __device__ __forceinline__ float hi_f(uint32_t x) { return __uint_as_float(x & 0xffff0000u); }
   static __device__ __forceinline__ uint32_t min2(uint32_t a, uint32_t b) {
     __nv_bfloat162 x, y;
     memcpy(&x, &a, 4); memcpy(&y, &b, 4);

@@ -838,7 +838,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 #pragma unroll
         for (int v = 0; v < 16; v += 2) {
           // (scale, zero) of tokens v and v + 1 -> (scale_v, scale_v+1)
-          const float2 sc = T::to_f2(prmt(sz[v], sz[v + 1], 0x5410u));
+          const float2 sc = make_float2(T::lo_f(sz[v]), T::lo_f(sz[v + 1]));
           const float2 pr = mul2(make_float2(s[qg][v], s[qg][v + 1]), sc);
           pp[v] = pr.x;
           pp[v + 1] = pr.y;
@@ -860,8 +860,8 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           yb[v] = __float_as_uint(fy.x);
           yb[v + 1] = __float_as_uint(fy.y);
           const float2 y = add2(fy, make_float2(-kMagicVal, -kMagicVal));
-          const uint32_t zz = prmt(sz[v], sz[v + 1], 0x7632u);   // zero-points of tokens v, v + 1
-          zv2 = fma2(T::to_f2(zz), y, zv2);
+          // zero-points of tokens v, v + 1
+          zv2 = fma2(make_float2(T::hi_f(sz[v]), T::hi_f(sz[v + 1])), y, zv2);
         }
         const float zv = zv2.x + zv2.y;
         st[qg].zs = __fmaf_rn(zv, dv, st[qg].zs);
