@@ -175,3 +175,24 @@ def test_large_context_properties():
                                      tail_k=cuda(tk), tail_v=cuda(tv), tail_len=cuda(tl))
     torch.cuda.synchronize()
     assert_close(out.cpu().numpy(), base)
+
+
+@pytest.mark.parametrize("splits", [0, 1, 3, 64])
+def test_fp16_heavy_batches_vs_oracle(splits, variant):
+    """Sequences whose fp16 region (sinks + tail) dominates, several with no quantised page
+    at all, mixed with paged ones.  The integer kernel slices the walk by cost units (an
+    fp16 chunk item counts as several pages), so with many splits some warps' slices lie
+    inside a chunk item's span and write neutral partials; the result must not depend on
+    that (checked against the oracle at every split count)."""
+    ctx = [32 + 127, 32 + 100, 32 + 3 * 128 + 127, 20, 32 + 64, 32 + 9 * 128 + 1]
+    tails = [127, 100, 127, 0, 64, 1]
+    case = synthetic.make_decode_case(211, len(ctx), 32, 8, 128, ctx, tails=tails)
+    total = sum(s.n_pages for s in case.seqs)
+    n_phys = total + 3
+    phys_of = GC.phys_layout(case, 211, n_phys)
+    pools = build_pools_gpu(case, phys_of, n_phys)
+    sk, sv, sl, tk, tv, tl = GC.padded_regions(case)
+    bt, npg = GC.block_table(case, phys_of)
+    exp = O.paged_attention_batched(case.q, bt, npg, tuple(p.cpu().numpy() for p in pools), case.boost_idx,
+                                    case.d_boost, sk, sv, sl, tk, tv, tl)
+    assert_close(run_batched(case, pools, phys_of, num_splits=splits), exp)
