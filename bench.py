@@ -56,7 +56,7 @@ METRIC = "quantized paged decode-attn HBM GB/s (% of peak) & tokens/s at 1/2/4/8
 MEASURED_TRAFFIC = {
     ("config2", "decode_i8_kernel"): 652_492_544 + 7_736_320,
     ("config2", "decode_mma_kernel"): 652_734_720 + 5_091_328,
-    ("config4", "decode_i8_kernel"): (641_469_184 + 4_378_880) * 8,
+    ("config4", "decode_i8_kernel"): (641_750_016 + 4_122_624) * 8,
 }
 
 def measured_traffic(workload, kernel, world):
