@@ -348,20 +348,17 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
   __half* ph = reinterpret_cast<__half*>(wsm + L.ptab);
   // q of query head g_ >> 1 (B column g_), channels 32 q_ .. 32 q_ + 31: the K
   // index (2q_, 2q_+1, 2q_+8, 2q_+9) of k-step s <-> channel 32 q_ + 4 s + (0..3)
+  // from the segment's q copy in shared memory (setup_segment: [group][half][prep lane], prep
+  // lane 8 head + channel block; zeros past the last query head)
   uint32_t qw[16];
   {
-    const int qh = qoff + (g_ >> 1);
-    if (qh < g) {
-      const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
-                                                        int64_t(h * g + qh) * a.q_s_head + 32 * q_);
+    const uint4* qs = reinterpret_cast<const uint4*>(wsm + L.qs + 1024 * (qoff >> 2));
+    const int l0 = 8 * (g_ >> 1) + 2 * q_;   // channels 32 q_ .. 32 q_ + 15 (block 2 q_), then block 2 q_ + 1
+    const uint4 x0 = qs[l0], x1 = qs[32 + l0], x2 = qs[l0 + 1], x3 = qs[32 + l0 + 1];
+    const uint4 xs[4] = {x0, x1, x2, x3};
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const uint4 x = src[i];
-        qw[4 * i] = x.x; qw[4 * i + 1] = x.y; qw[4 * i + 2] = x.z; qw[4 * i + 3] = x.w;
-      }
-    } else {
-#pragma unroll
-      for (int i = 0; i < 16; ++i) qw[i] = 0u;
+    for (int i = 0; i < 4; ++i) {
+      qw[4 * i] = xs[i].x; qw[4 * i + 1] = xs[i].y; qw[4 * i + 2] = xs[i].z; qw[4 * i + 3] = xs[i].w;
     }
   }
   for (int f0 = t_begin; f0 < t_end; f0 += kG) {
@@ -377,6 +374,13 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
       return key ? reinterpret_cast<const uint16_t*>(a.tail_k) + cr * a.tk_s_seq + h * a.tk_s_head + tt * a.tk_s_tok
                  : reinterpret_cast<const uint16_t*>(a.tail_v) + cr * a.tv_s_seq + h * a.tv_s_head + tt * a.tv_s_tok;
     };
+    // every key and value row of this pass into L1 first (two 128-byte lines per row, one
+    // line per lane and request): the tile loads below then wait on one round trip, not one
+    // per tile
+    for (int i = lane; i < 2 * ntok; i += 32) {
+      prefetch_l1(row(true, i >> 1) + 64 * (i & 1));
+      prefetch_l1(row(false, i >> 1) + 64 * (i & 1));
+    }
     // scores: tile m rows g_ / g_ + 8 <-> tokens 16 m + g_ / 16 m + g_ + 8 (s[2 m], s[2 m + 1])
     float s[16];
 #pragma unroll
