@@ -54,7 +54,7 @@ METRIC = "quantized paged decode-attn HBM GB/s (% of peak) & tokens/s at 1/2/4/8
 # and kernel; None where no capture exists.  Config 4 was captured at batch 8
 # (`--batch 8`, 1/8 of the page-heads) and scaled by 8: its traffic is per page-head.
 MEASURED_TRAFFIC = {
-    ("config2", "decode_i8_kernel"): 652_492_544 + 7_736_320,
+    ("config2", "decode_i8_kernel"): 652_503_552 + 4_320_256,
     ("config2", "decode_mma_kernel"): 652_734_720 + 5_091_328,
     ("config4", "decode_i8_kernel"): (641_750_016 + 4_122_624) * 8,
 }
