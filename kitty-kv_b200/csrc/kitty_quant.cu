@@ -389,35 +389,29 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
     }
   }
   __syncthreads();
-  if (tid < 64) {  // channel pair tid: channels 2*tid, 2*tid+1
-    uint32_t a2 = s_red[0][tid][0], b2 = s_red[0][tid][1];
+  if (tid < D) {  // channel tid (one per thread: the divisions below run 128-wide, not 64)
+    const int c = tid, pr = c >> 1;
+    uint32_t a2 = s_red[0][pr][0], b2 = s_red[0][pr][1];
 #pragma unroll
     for (int w = 1; w < 8; ++w) {
-      a2 = T::min2(a2, s_red[w][tid][0]);
-      b2 = T::max2(b2, s_red[w][tid][1]);
+      a2 = T::min2(a2, s_red[w][pr][0]);
+      b2 = T::max2(b2, s_red[w][pr][1]);
     }
-    const float2 mn2 = T::to_f2(a2), mx2 = T::to_f2(b2);
+    const float mnf = (c & 1) ? T::hi_f(a2) : T::lo_f(a2);
+    const float mxf = (c & 1) ? T::hi_f(b2) : T::lo_f(b2);
     uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.key_scale) + page * a.meta_s_page + h * a.meta_s_head;
     uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.key_zero) + page * a.meta_s_page + h * a.meta_s_head;
-    bool nonfinite = false;
-#pragma unroll
-    for (int e = 0; e < 2; ++e) {
-      const int c = 2 * tid + e;
-      const float mnf = e ? mn2.y : mn2.x;
-      const float mxf = e ? mx2.y : mx2.x;
-      const int r = bidx[c];
-      const bool boosted = r < a.sentinel;
-      const float maxq = boosted ? 15.0f : 3.0f;
-      const float scale = __fdiv_rn(clamp_min(mxf - mnf, 1e-8f), maxq);
-      float zp = rintf(__fdiv_rn(-mnf, scale));
-      zp = tmin(tmax(zp, 0.0f), maxq);
-      s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq; s_r[c] = __frcp_rn(scale);
-      s_row[c] = (boosted && r < K) ? r : -1;
-      nonfinite |= !(isfinite(mnf) && isfinite(mxf) && isfinite(scale));
-      out_scale[c] = Half16<kMetaBf16>::meta(scale);
-      out_zero[c] = Half16<kMetaBf16>::meta(zp);
-    }
-    if (nonfinite) s_nonfinite = 1;
+    const int r = bidx[c];
+    const bool boosted = r < a.sentinel;
+    const float maxq = boosted ? 15.0f : 3.0f;
+    const float scale = __fdiv_rn(clamp_min(mxf - mnf, 1e-8f), maxq);
+    float zp = rintf(__fdiv_rn(-mnf, scale));
+    zp = tmin(tmax(zp, 0.0f), maxq);
+    s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq; s_r[c] = __frcp_rn(scale);
+    s_row[c] = (boosted && r < K) ? r : -1;
+    out_scale[c] = Half16<kMetaBf16>::meta(scale);
+    out_zero[c] = Half16<kMetaBf16>::meta(zp);
+    if (!(isfinite(mnf) && isfinite(mxf) && isfinite(scale))) s_nonfinite = 1;
   }
   __syncthreads();
 
