@@ -313,6 +313,62 @@ def decode_call(w, q=None, bt=None, npg=None, out=None):
         tail_v=w["tail_v"], tail_len=w["tail_len"], out=out, max_pages_per_seq=w["n_pages"])
 
 
+ATOL, RTOL = 2e-3, 1e-2   # fp16 output tolerance for attention (atol 2e-3 / rtol 1e-2)
+
+
+def oracle_sample(layout, k=2):
+    """Rows of a decode batch whose outputs are checked against the oracle: the first
+    row and the row with the most pages (the last row when all are equal), plus the
+    shortest row for mixed-length batches."""
+    if not layout:
+        return []
+    rows = [0, max(range(len(layout)), key=lambda i: (layout[i][0], i))]
+    if len({n for n, _ in layout}) > 1:
+        rows.append(min(range(len(layout)), key=lambda i: (layout[i][0], i)))
+    return sorted(set(rows))[:max(k, 1) + 1]
+
+
+def oracle_check(w, out, rows):
+    """Compare rows of a decode output (B, Hq, D) with the numpy oracle (the CPU
+    restatement of the reference's paged_attention_reference,
+    kitty/kernels/attention.py:46-189) on the same pools, every query head.  The
+    row's pages are read back from the resident pools in block-table order.  Returns
+    the worst |got - exp| / (atol + rtol |exp|) over the rows (<= 1 passes) and the
+    worst absolute error.  The KV heads of a row are independent (query head qh reads
+    KV head qh // g), so the oracle runs one KV head per host thread."""
+    import concurrent.futures as cf
+    import numpy as np
+    from oracle import kitty_oracle as O
+    bidx = w["bidx"].cpu().numpy()
+    tails = w["tail_len"]
+    H, Hq, D = w["H"], w["Hq"], w["D"]
+    g = Hq // H
+    jobs = []
+    for i in rows:
+        n, t = w["layout"][i]
+        assert isinstance(tails, int) or int(tails[i].item()) == t
+        idx = w["bt"][i, :n].long()
+        pools = [p.index_select(0, idx).cpu().numpy() for p in w["pools"]]
+        q = w["q"][i].cpu().numpy()
+        reg = [w["sink_k"][i].cpu().numpy(), w["sink_v"][i].cpu().numpy(),
+               w["tail_k"][i, :, :t].cpu().numpy(), w["tail_v"][i, :, :t].cpu().numpy()]
+        got = out[i].float().cpu().numpy()
+        for h in range(H):
+            jobs.append((q[h * g:(h + 1) * g], [np.ascontiguousarray(p[:, h:h + 1]) for p in pools],
+                         bidx[h:h + 1], [r[h:h + 1] for r in reg], got[h * g:(h + 1) * g]))
+
+    def one(job):
+        q, pools, b, reg, got = job
+        exp = O.paged_attention(q, list(range(pools[0].shape[0])), *pools, b, w["K"], *reg, g, 1, D)
+        err = np.abs(got - exp.astype(np.float32))
+        ratio = err / (ATOL + RTOL * np.abs(exp.astype(np.float32)))
+        return float(np.nan_to_num(ratio, nan=np.inf).max()), float(np.nan_to_num(err, nan=np.inf).max())
+
+    with cf.ThreadPoolExecutor(max_workers=max(1, min(len(jobs), os.cpu_count() or 1))) as ex:
+        res = list(ex.map(one, jobs))
+    return max((r for r, _ in res), default=0.0), max((a for _, a in res), default=0.0)
+
+
 def build_quantize_workload(spec, device, seed):
     """fp16 prefill keys and values (B, H, T, D) and empty pools for every page-head."""
     import torch
@@ -457,7 +513,8 @@ def reference_arm(args, spec):
             "vs_baseline": None, "dtype": "f32", "data": "synthetic",
             "config": {"workload": args.workload, **spec, "sample_sequences": n_seq},
             "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": workers, "kind": "port",
-                             "sample": f"{label}, (sequence, KV head) units on a host thread pool"},
+                             "sample": f"{label}, (sequence, KV head) units on a host thread pool",
+                             **host_cores(), "reference_own_path": reference_timing()},
             "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
     if spec["kind"] == "decode":
         line["tokens_per_s"] = round(n_seq / sec, 3)
@@ -474,7 +531,22 @@ def cpu_baseline(spec, workload):
     sec = sum(runner.run(units) for _ in range(reps)) / reps
     runner.close()
     return {"value": round(cbytes / sec / 1e9, 4), "unit": "GB/s", "cores": workers, "kind": "port",
-            "sample": f"{label}, mean of {reps} runs"}
+            "sample": f"{label}, mean of {reps} runs", **host_cores(), "reference_own_path": reference_timing()}
+
+
+def host_cores():
+    """The host's logical CPUs and torch's intra-op thread count, beside the worker
+    threads the CPU leg used (``cores``)."""
+    import torch
+    return {"host_cpus": os.cpu_count(), "torch_threads": torch.get_num_threads()}
+
+
+def reference_timing():
+    """The reference's own CPU decode (paged_attention_reference) against this numpy
+    restatement on one config-1 step, as recorded by tests/golden/time_reference.py
+    where the reference is importable (it is not installed on the GPU box)."""
+    p = ROOT / "tests" / "golden" / "reference_timing.json"
+    return json.loads(p.read_text()) if p.exists() else None
 
 
 # ---------------------------------------------------------------------------
@@ -558,37 +630,61 @@ def decode_arm(args, spec, d, device, local):
     nbytes_local = decode_bytes(w["layout"], Hq, H, D, G, K)
     nbytes_total = nbytes_local * world if replica else d.reduce(nbytes_local, d.dist.ReduceOp.SUM)
     stream = torch.cuda.current_stream(device)
-    out = torch.empty(B, Hq, D, dtype=torch.float16, device=device)
     gather = spec["shard"] == "kv_head" and world > 1
     if gather:
+        # the decode writes this rank's heads head-major, (Hq_local, B, D), through the
+        # output strides, straight into the buffer the all-gather sends; the gathered
+        # (Hq, B, D) buffer needs no reordering either
         from kitty.distributed import gather_head_outputs
+        out_hm = torch.empty(Hq, B, D, dtype=torch.float16, device=device)
+        out = out_hm.permute(1, 0, 2)
+        full = torch.empty(world * Hq, B, D, dtype=torch.float16, device=device)
+    else:
+        out = torch.empty(B, Hq, D, dtype=torch.float16, device=device)
+
+    def eager_step():
+        decode_call(w, out=out)
+        if gather:
+            gather_head_outputs(out_hm, full=full)
 
     for _ in range(args.warmup):
-        decode_call(w, out=out)
+        eager_step()
     torch.cuda.synchronize(device)
-    # device-resident steps replay the decode launches from a CUDA graph (no host work
-    # between steps); the all-gather of the tensor-parallel configuration runs eagerly
-    launch_mode = "cuda graph replay"
-    try:
-        graph = torch.cuda.CUDAGraph()
+    # device-resident steps replay the step from CUDA graphs (no host work between
+    # steps): the decode launches, and for the tensor-parallel configuration the NCCL
+    # all-gather captured in the same graph
+    def capture(fn):
+        g = torch.cuda.CUDAGraph()
         cap = torch.cuda.Stream(device)
         cap.wait_stream(stream)
         with torch.cuda.stream(cap):
-            decode_call(w, out=out)          # first call on this stream sets up its workspace
+            fn()                             # first call on this stream sets up its workspace
             torch.cuda.synchronize(device)
-            with torch.cuda.graph(graph, stream=cap):
-                decode_call(w, out=out)
+            with torch.cuda.graph(g, stream=cap):
+                fn()
         stream.wait_stream(cap)
-        run_decode = graph.replay
+        torch.cuda.synchronize(device)
+        return g
+
+    graphs = []
+    g_decode = g_step = None
+    launch_mode = "cuda graph replay" + (" (decode + all-gather in one graph)" if gather else "")
+    try:
+        g_decode = capture(lambda: decode_call(w, out=out))
+        graphs.append(g_decode)
+        run_decode = g_decode.replay
     except Exception as e:   # capture unavailable: eager launches
         launch_mode = f"eager ({type(e).__name__})"
-        graph = None
         run_decode = lambda: decode_call(w, out=out)
-
-    def step():
-        run_decode()
-        if gather:
-            gather_head_outputs(out.permute(1, 0, 2).contiguous())
+    step = run_decode
+    if gather:
+        try:
+            g_step = capture(eager_step)
+            graphs.append(g_step)
+            step = g_step.replay
+        except Exception as e:
+            launch_mode += f"; all-gather eager ({type(e).__name__})"
+            step = lambda: (run_decode(), gather_head_outputs(out_hm, full=full))
 
     for _ in range(args.warmup):
         step()
@@ -596,10 +692,15 @@ def decode_arm(args, spec, d, device, local):
     with ClockSampler(local) as clocks:
         ms, _ = timed(stream, args.steps, step, torch, device, d)
     decode_ms, launch_ms = timed(stream, args.steps, run_decode, torch, device, d)
+    gather_ms = None
+    if gather:
+        gather_ms, _ = timed(stream, args.steps, lambda: gather_head_outputs(out_hm, full=full), torch, device, d)
+    step_out = full if gather else out      # the step's result: the gathered heads under TP
 
     # ---- end to end through the public API with host buffers: a step's inputs (q, block
     # table, page counts) sit in one pinned staging buffer and cross to the device in one
-    # copy (as a serving loop would stage them); the output comes back in another
+    # copy (as a serving loop would stage them); the output comes back in another (under
+    # tensor parallelism the gathered output of all heads, head-major)
     def pack(ts):
         parts = [t.cpu().contiguous().view(torch.uint8).reshape(-1) for t in ts]
         host = torch.empty(sum(p.numel() for p in parts), dtype=torch.uint8).pin_memory()
@@ -611,23 +712,42 @@ def decode_arm(args, spec, d, device, local):
         return host, views
     in_host, in_views = pack([w["q"], w["bt"], w["npg"]])
     in_dev = torch.empty_like(in_host, device=device)
-    out_host = torch.empty(B, Hq, D, dtype=torch.float16).pin_memory()
+    out_host = torch.empty(tuple(step_out.shape), dtype=torch.float16).pin_memory()
     h2d = in_host.numel()
     d2h = out_host.numel() * 2
+    if gather:
+        e2e_hm = torch.empty(Hq, B, D, dtype=torch.float16, device=device)
+        e2e_full = torch.empty_like(full)
 
     def e2e_step():
         in_dev.copy_(in_host, non_blocking=True)
         q, bt, npg = (in_dev[at:at + n].view(dt).view(shape) for at, n, dt, shape in in_views)
-        o = decode_call(w, q=q, bt=bt, npg=npg)
         if gather:
-            gather_head_outputs(o.permute(1, 0, 2).contiguous())
-        out_host.copy_(o, non_blocking=True)
+            decode_call(w, q=q, bt=bt, npg=npg, out=e2e_hm.permute(1, 0, 2))
+            gather_head_outputs(e2e_hm, full=e2e_full)
+            out_host.copy_(e2e_full, non_blocking=True)
+        else:
+            out_host.copy_(decode_call(w, q=q, bt=bt, npg=npg), non_blocking=True)
 
     for _ in range(args.warmup):
         e2e_step()
     torch.cuda.synchronize(device)
     e2e_ms, _ = timed(stream, args.steps, e2e_step, torch, device, d)
-    ok = bool(torch.isfinite(out).all().item()) and bool(torch.equal(out.cpu(), out_host))
+    same = bool(torch.equal(step_out.cpu(), out_host))
+    # graphs holding NCCL calls are released before the process group is destroyed
+    step = run_decode = g_decode = g_step = None
+    graphs.clear()
+    # the timed output against the oracle on sampled rows of this rank's batch
+    check = None
+    if rank == 0:
+        rows = oracle_sample(w["layout"])
+        t0 = time.perf_counter()
+        ratio, abs_err = oracle_check(w, out, rows)
+        check = {"vs": "numpy oracle (restatement of the reference's paged_attention_reference)",
+                 "rows": rows, "query_heads": Hq, "atol": ATOL, "rtol": RTOL,
+                 "max_abs_err": round(abs_err, 6), "max_err_over_tol": round(ratio, 4),
+                 "pass": bool(ratio <= 1.0) and same, "e2e_equals_device_resident": same,
+                 "check_s": round(time.perf_counter() - t0, 2)}
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -666,10 +786,11 @@ def decode_arm(args, spec, d, device, local):
         "cpu_baseline": cpu,
         "clocks": clocks.summary(),
         "gpu_launches": 2 * args.steps,
-        "output_check": "finite and identical between device-resident and e2e runs" if ok else "FAILED",
+        "output_check": check,
     }
     if gather:
         line["decode_only_ms_per_step"] = round(decode_ms, 4)
+        line["all_gather_ms_per_step"] = round(gather_ms, 4)
     return line
 
 

@@ -38,7 +38,7 @@ extern "C" {
 #define KITTY_ERR_CUDA 3             /* a CUDA runtime call failed */
 #define KITTY_ERR_WORKSPACE 4        /* workspace missing or too small */
 
-#define KITTY_ABI_VERSION 3
+#define KITTY_ABI_VERSION 4
 
 /* 16-bit floating-point type of the fp16 tensors of a call (the `dtype` field
  * of the argument structs; 0 = the zero-initialised default).  With bf16 the
@@ -53,6 +53,10 @@ extern "C" {
 /* quantisers only: bf16 source, fp16 scale / zero-point (what the reference's
  * functional quantize_*_page_torch returns for a bf16 input) */
 #define KITTY_DTYPE_BF16_F16META 3
+/* dequantisers only: fp16 (4) or bf16 (5) scale / zero-point and a float32
+ * output, as the reference's functional dequantize_*_page_torch return */
+#define KITTY_DTYPE_F16_F32OUT 4
+#define KITTY_DTYPE_BF16_F32OUT 5
 
 /* ABI version compiled into the library (KITTY_ABI_VERSION). */
 int kitty_abi_version(void);
@@ -63,7 +67,7 @@ const char* kitty_last_error(void);
 /* sizeof() of the argument structs below, so a foreign-function binding can
  * check its mirror of them: kind 0 = KittyKeyQuantArgs, 1 = KittyValueQuantArgs,
  * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs, 4 = KittyCacheState,
- * 5 = KittyPrefillArgs; 0 for an unknown kind. */
+ * 5 = KittyPrefillArgs, 6 = KittyValueDequantArgs; 0 for an unknown kind. */
 size_t kitty_args_size(int kind);
 
 /* ---------------------------------------------------------------------------
@@ -135,7 +139,9 @@ int kitty_quantize_value_pages(const KittyValueQuantArgs* args, void* stream);
 /* ---------------------------------------------------------------------------
  * Key page dequantisation to fp16 (D, G) blocks: x = (code - zp) * scale in fp32,
  * code = low | (high << 2) for channels with boost_idx < d_boost.
- * Replaces dequantize_key_page (kitty/kernels/dequantize_key.py:169-228).
+ * Replaces dequantize_key_page (kitty/kernels/dequantize_key.py:169-228) and,
+ * with dtype KITTY_DTYPE_F16_F32OUT / BF16_F32OUT (float32 out),
+ * dequantize_key_page_torch (kitty/kernels/dequantize_key.py:35-97).
  * Job j's output element (c, t) is at out + out_off[j] + c*out_s_ch + t*out_s_tok.
  * Source page-head: (src_page[j], head[j]).
  * ------------------------------------------------------------------------- */
@@ -153,10 +159,38 @@ typedef struct KittyKeyDequantArgs {
   const int64_t* out_off;     /* [n_jobs] */
   int64_t out_s_ch, out_s_tok;
   int32_t n_jobs, num_heads, head_dim, group, d_boost;
-  int32_t dtype;              /* KITTY_DTYPE_*: key_scale / key_zero and out */
+  int32_t dtype;              /* KITTY_DTYPE_*: key_scale / key_zero and out (F32OUT: float32 out) */
 } KittyKeyDequantArgs;
 
 int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream);
+
+/* ---------------------------------------------------------------------------
+ * Value page dequantisation: x = (code - zp_t) * scale_t in fp32 for every
+ * token t and channel c of a (G, D/4) packed page-head.
+ * Replaces dequantize_value_page_torch (kitty/kernels/quantize_value.py:97-133):
+ * dtype KITTY_DTYPE_F16_F32OUT / BF16_F32OUT give its float32 (G, D) block;
+ * KITTY_DTYPE_F16 / BF16 round the result to the metadata's 16-bit type.
+ * Job j reads page-head (src_page[j], head[j]); the scale and zero-point of
+ * token t are at val_scale / val_zero + src_page*meta_s_page + head*meta_s_head
+ * + t*meta_s_tok (meta_s_tok = 2 for the interleaved value_metadata pool).
+ * Output element (t, c) is at out + out_off[j] + t*out_s_tok + c*out_s_ch.
+ * ------------------------------------------------------------------------- */
+typedef struct KittyValueDequantArgs {
+  const uint8_t* val_codes;
+  const void* val_scale;      /* usually value_metadata */
+  const void* val_zero;       /* usually value_metadata + 1 element */
+  int64_t codes_s_page, codes_s_head;
+  int64_t meta_s_page, meta_s_head, meta_s_tok;
+  const int32_t* src_page;    /* [n_jobs] (device memory) */
+  const int32_t* head;        /* [n_jobs] (device memory) */
+  void* out;
+  const int64_t* out_off;     /* [n_jobs] (device memory) */
+  int64_t out_s_tok, out_s_ch;
+  int32_t n_jobs, head_dim, group;
+  int32_t dtype;              /* KITTY_DTYPE_F16 / BF16 / F16_F32OUT / BF16_F32OUT */
+} KittyValueDequantArgs;
+
+int kitty_dequantize_value_pages(const KittyValueDequantArgs* args, void* stream);
 
 /* ---------------------------------------------------------------------------
  * Fused paged GQA decode attention over the quantised pools plus the fp16
@@ -231,10 +265,12 @@ int kitty_paged_decode(const KittyDecodeArgs* args, void* stream);
  * kernels as kitty_paged_decode but ignores args->workspace and keeps the
  * split partial results in a static 8 MiB device array inside the library
  * (held on every GPU that loads the library until exit).  The first call on a
- * device looks the array up (make it before any stream capture); all calls
- * share it, so calls that overlap on the GPU race.  With num_splits == 0 the
- * split count is lowered until the partials fit; an explicit num_splits that
- * does not fit returns KITTY_ERR_WORKSPACE.  Allocates nothing. */
+ * device looks the array up (make it before any stream capture) and caches
+ * the address for the life of the process, so do not call it after
+ * cudaDeviceReset; all calls share the array, so calls that overlap on the
+ * GPU race.  With num_splits == 0 the split count is lowered to the largest
+ * that fits; an explicit num_splits that does not fit returns
+ * KITTY_ERR_WORKSPACE.  Allocates nothing. */
 int kitty_paged_decode_noalloc(const KittyDecodeArgs* args, void* stream);
 
 /* ---------------------------------------------------------------------------

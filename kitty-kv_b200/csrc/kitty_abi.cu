@@ -11,6 +11,7 @@ namespace kitty {
 int quantize_key_pages_impl(const KittyKeyQuantArgs* a, void* stream);
 int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream);
 int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream);
+int dequantize_value_pages_impl(const KittyValueDequantArgs* a, void* stream);
 int read_cache_error(uint32_t* flags, int clear);
 
 namespace {
@@ -131,6 +132,7 @@ size_t kitty_args_size(int kind) {
     case 3: return sizeof(KittyDecodeArgs);
     case 4: return sizeof(KittyCacheState);
     case 5: return sizeof(KittyPrefillArgs);
+    case 6: return sizeof(KittyValueDequantArgs);
     default: return 0;
   }
 }
@@ -148,6 +150,11 @@ int kitty_quantize_value_pages(const KittyValueQuantArgs* args, void* stream) {
 int kitty_dequantize_key_pages(const KittyKeyDequantArgs* args, void* stream) {
   clear_error();
   return dequantize_key_pages_impl(args, stream);
+}
+
+int kitty_dequantize_value_pages(const KittyValueDequantArgs* args, void* stream) {
+  clear_error();
+  return dequantize_value_pages_impl(args, stream);
 }
 
 int kitty_device_error_flags(uint32_t* flags, int clear) {

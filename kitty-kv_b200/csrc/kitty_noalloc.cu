@@ -14,14 +14,17 @@
 //   * every GPU that loads the library holds the 8 MiB until the process exits;
 //   * its device address is looked up once per device, on the first call made
 //     with that device current (cudaGetSymbolAddress); make that first call
-//     before any stream capture;
+//     before any stream capture.  The address is cached for the life of the
+//     process: after cudaDeviceReset (or any teardown of the device's primary
+//     context) the module is loaded again and the cached address is stale, so
+//     do not call this entry point after resetting a device;
 //   * all calls share it, and it keeps the previous call's contents.  Nothing in
 //     it needs to start at zero: every split writes all of its partial results
 //     before the merge kernel reads them.  Calls whose kernels overlap on the GPU
 //     (different streams, or other threads) race on it; order them.
-//   * when the library picks the split count (num_splits == 0) it is lowered
-//     until the partials fit; an explicit num_splits whose partials do not fit
-//     is rejected with KITTY_ERR_WORKSPACE.
+//   * when the library picks the split count (num_splits == 0) it is lowered to
+//     the largest count whose partials fit; an explicit num_splits whose
+//     partials do not fit is rejected with KITTY_ERR_WORKSPACE.
 // No cudaMalloc, cudaFree or allocating library call is made.
 
 #include <mutex>
@@ -74,16 +77,34 @@ extern "C" int kitty_paged_decode_noalloc(const KittyDecodeArgs* args, void* str
                              std::to_string(need) + " bytes of scratch; the static scratch holds " +
                              std::to_string(kNoAllocScratchBytes) + " (pass num_splits=0 to let it fit)");
     }
-    // lower the requested split count until the partial results fit
-    for (int32_t target = splits - 1; target >= 1 && need > kNoAllocScratchBytes; --target) {
-      a.num_splits = target;
-      rc = kitty_paged_decode_workspace_size(&a, &need, &splits);
+    // the largest requested split count whose partials fit: the plan's slot count, and
+    // so the bytes, never shrink as the request grows, so a binary search over
+    // [1, splits - 1] checks about log2(splits) plans instead of stepping down by one
+    int32_t lo = 1, hi = splits - 1, best = 0;
+    size_t best_need = 0, tried_need = need;
+    int32_t tried_splits = splits;
+    while (lo <= hi) {
+      const int32_t mid = lo + (hi - lo) / 2;
+      a.num_splits = mid;
+      size_t n = 0;
+      int32_t s = 0;
+      rc = kitty_paged_decode_workspace_size(&a, &n, &s);
       if (rc != KITTY_OK) return rc;
+      if (n <= kNoAllocScratchBytes) {
+        best = mid, best_need = n;
+        lo = mid + 1;
+      } else {
+        tried_need = n, tried_splits = s;
+        hi = mid - 1;
+      }
     }
-    if (need > kNoAllocScratchBytes)
-      return kitty::fail(KITTY_ERR_WORKSPACE, "paged_decode_noalloc: even one split needs " + std::to_string(need) +
-                                                  " bytes of scratch; the static scratch holds " +
-                                                  std::to_string(kNoAllocScratchBytes));
+    if (best == 0)
+      return kitty::fail(KITTY_ERR_WORKSPACE,
+                         "paged_decode_noalloc: the smallest split plan (" + std::to_string(tried_splits) +
+                             " partial slots per sequence and KV head) needs " + std::to_string(tried_need) +
+                             " bytes of scratch; the static scratch holds " + std::to_string(kNoAllocScratchBytes));
+    a.num_splits = best;
+    need = best_need;
   }
   void* scratch = nullptr;
   if (need > 0) {

@@ -201,7 +201,14 @@ quantize_value_kernel(const KittyValueQuantArgs a) {
   }
 }
 
-template <bool kBf16>
+// Element store of the dequantisers: the metadata's 16-bit type, or float32.
+template <bool kBf16, bool kF32Out>
+__device__ __forceinline__ void store_dq(void* out, int64_t idx, float x) {
+  if constexpr (kF32Out) reinterpret_cast<float*>(out)[idx] = x;
+  else reinterpret_cast<uint16_t*>(out)[idx] = Half16<kBf16>::from_f(x);
+}
+
+template <bool kBf16, bool kF32Out>
 __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
   using T = Half16<kBf16>;
   const int D = a.head_dim, G = a.group, K = a.d_boost, G4 = G / 4;
@@ -213,7 +220,7 @@ __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
   const uint16_t* sc = reinterpret_cast<const uint16_t*>(a.key_scale) + page * a.meta_s_page + h * a.meta_s_head;
   const uint16_t* zr = reinterpret_cast<const uint16_t*>(a.key_zero) + page * a.meta_s_page + h * a.meta_s_head;
   const uint8_t* bidx = a.boost_idx + h * a.bidx_s_head;
-  uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + a.out_off[job];
+  const int64_t base = a.out_off[job];
   // dequantize_key.py:69-97: code = low | (high << 2) when boost_idx < d_boost.
   for (int i = threadIdx.x; i < D * G4; i += blockDim.x) {
     const int c = i / G4;
@@ -225,8 +232,35 @@ __global__ void dequantize_key_kernel(const KittyKeyDequantArgs a) {
 #pragma unroll
     for (int k = 0; k < 4; ++k) {
       const uint32_t code = ((lo >> (2 * k)) & 3u) | (((hi >> (2 * k)) & 3u) << 2);
-      const float x = (static_cast<float>(code) - z) * s;
-      out[c * a.out_s_ch + (4 * j + k) * a.out_s_tok] = T::from_f(x);
+      const float x = __fmul_rn(__fsub_rn(static_cast<float>(code), z), s);
+      store_dq<kBf16, kF32Out>(a.out, base + c * a.out_s_ch + (4 * j + k) * a.out_s_tok, x);
+    }
+  }
+}
+
+// quantize_value.py:122-133: codes unpacked per token (byte j of token t holds
+// channels 4j..4j+3 at bits 0,2,4,6), x = (code - zp_t) * scale_t in float32.
+template <bool kBf16, bool kF32Out>
+__global__ void dequantize_value_kernel(const KittyValueDequantArgs a) {
+  using T = Half16<kBf16>;
+  const int D4 = a.head_dim / 4, G = a.group;
+  const int job = blockIdx.x;
+  const int64_t page = a.src_page[job];
+  const int h = a.head[job];
+  const uint8_t* codes = a.val_codes + page * a.codes_s_page + h * a.codes_s_head;
+  const int64_t m0 = page * a.meta_s_page + h * a.meta_s_head;
+  const uint16_t* sc = reinterpret_cast<const uint16_t*>(a.val_scale) + m0;
+  const uint16_t* zr = reinterpret_cast<const uint16_t*>(a.val_zero) + m0;
+  const int64_t base = a.out_off[job];
+  for (int i = threadIdx.x; i < G * D4; i += blockDim.x) {
+    const int t = i / D4;
+    const int j = i - t * D4;
+    const uint32_t byte = codes[i];
+    const float s = T::to_f(sc[int64_t(t) * a.meta_s_tok]), z = T::to_f(zr[int64_t(t) * a.meta_s_tok]);
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const float x = __fmul_rn(__fsub_rn(static_cast<float>((byte >> (2 * k)) & 3u), z), s);
+      store_dq<kBf16, kF32Out>(a.out, base + t * a.out_s_tok + (4 * j + k) * a.out_s_ch, x);
     }
   }
 }
@@ -664,6 +698,15 @@ int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream) {
   return check_launch("quantize_value_kernel");
 }
 
+namespace {
+// metadata type and output type of a dequantiser call: (bf16 metadata, float32 out)
+bool dequant_types(int32_t dt, bool* bf16, bool* f32) {
+  *bf16 = dt == KITTY_DTYPE_BF16 || dt == KITTY_DTYPE_BF16_F32OUT;
+  *f32 = dt == KITTY_DTYPE_F16_F32OUT || dt == KITTY_DTYPE_BF16_F32OUT;
+  return dt == KITTY_DTYPE_F16 || dt == KITTY_DTYPE_BF16 || *f32;
+}
+}  // namespace
+
 int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream) {
   if (!a) return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_key_pages: args is NULL");
   if (a->n_jobs == 0) return KITTY_OK;
@@ -672,11 +715,31 @@ int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream) {
   if (!a->key_low || !a->key_scale || !a->key_zero || !a->src_page || !a->head || !a->boost_idx || !a->out ||
       !a->out_off || (a->d_boost > 0 && !a->key_high))
     return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_key_pages: NULL pointer");
-  if (a->dtype != KITTY_DTYPE_F16 && a->dtype != KITTY_DTYPE_BF16)
-    return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_key_pages: dtype must be KITTY_DTYPE_F16 or KITTY_DTYPE_BF16");
-  if (a->dtype == KITTY_DTYPE_BF16) dequantize_key_kernel<true><<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
-  else dequantize_key_kernel<false><<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
+  bool bf16 = false, f32 = false;
+  if (!dequant_types(a->dtype, &bf16, &f32))
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_key_pages: dtype must be KITTY_DTYPE_F16, BF16, "
+                                            "F16_F32OUT or BF16_F32OUT");
+  auto kern = bf16 ? (f32 ? dequantize_key_kernel<true, true> : dequantize_key_kernel<true, false>)
+                   : (f32 ? dequantize_key_kernel<false, true> : dequantize_key_kernel<false, false>);
+  kern<<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
   return check_launch("dequantize_key_kernel");
+}
+
+int dequantize_value_pages_impl(const KittyValueDequantArgs* a, void* stream) {
+  if (!a) return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_value_pages: args is NULL");
+  if (a->n_jobs == 0) return KITTY_OK;
+  if (a->n_jobs < 0 || a->head_dim <= 0 || a->head_dim % 4 != 0 || a->group <= 0)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_value_pages: bad sizes");
+  if (!a->val_codes || !a->val_scale || !a->val_zero || !a->src_page || !a->head || !a->out || !a->out_off)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_value_pages: NULL pointer");
+  bool bf16 = false, f32 = false;
+  if (!dequant_types(a->dtype, &bf16, &f32))
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "dequantize_value_pages: dtype must be KITTY_DTYPE_F16, BF16, "
+                                            "F16_F32OUT or BF16_F32OUT");
+  auto kern = bf16 ? (f32 ? dequantize_value_kernel<true, true> : dequantize_value_kernel<true, false>)
+                   : (f32 ? dequantize_value_kernel<false, true> : dequantize_value_kernel<false, false>);
+  kern<<<a->n_jobs, 256, 0, as_stream(stream)>>>(*a);
+  return check_launch("dequantize_value_kernel");
 }
 
 }  // namespace kitty

@@ -63,13 +63,23 @@ def sequence_costs(num_pages: Sequence[int], sink_lens: Sequence[int], tail_lens
             for n, s, t in zip(num_pages, sink_lens, tail_lens)]
 
 
-def gather_head_outputs(out_local: torch.Tensor, group=None) -> torch.Tensor:
-    """All-gather per-rank head-major outputs ``(Hq_local, B, D)`` into ``(B, Hq, D)``.
+def gather_head_outputs(out_local: torch.Tensor, group=None, full: torch.Tensor = None) -> torch.Tensor:
+    """All-gather per-rank head-major outputs ``(Hq_local, B, D)`` into the head-major
+    buffer ``full`` ``(Hq, B, D)`` (allocated when not given; pass one to keep the call
+    free of allocation, e.g. inside a CUDA graph) and return it viewed as ``(B, Hq, D)``.
 
-    Rank r's heads land at ``[r*Hq_local, (r+1)*Hq_local)``."""
+    Rank r's heads land at ``[r*Hq_local, (r+1)*Hq_local)``.  The returned tensor is
+    ``full.permute(1, 0, 2)``: a strided view (strides ``(D, B*D, 1)``), not a
+    contiguous tensor; call ``.contiguous()`` where a dense ``(B, Hq, D)`` is needed.
+    The decode entry points accept it as ``out`` directly (they take any head and
+    sequence strides), and a rank's own decode can write its ``(Hq_local, B, D)``
+    slice head-major the same way, so no copy is needed on either side."""
     world = dist.get_world_size(group)
     hq_local, B, D = out_local.shape
-    full = torch.empty(world * hq_local, B, D, dtype=out_local.dtype, device=out_local.device)
+    if full is None:
+        full = torch.empty(world * hq_local, B, D, dtype=out_local.dtype, device=out_local.device)
+    elif tuple(full.shape) != (world * hq_local, B, D) or not full.is_contiguous():
+        raise RuntimeError("full must be a contiguous (world * Hq_local, B, D) tensor")
     dist.all_gather_into_tensor(full, out_local.contiguous(), group=group)
     return full.permute(1, 0, 2)
 

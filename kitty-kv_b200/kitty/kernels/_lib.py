@@ -16,7 +16,7 @@ from typing import Dict, Optional, Tuple
 
 import torch
 
-ABI_VERSION = 3
+ABI_VERSION = 4
 LIB_NAME = "libkitty_b200.so"
 _LIB_PATH = Path(os.environ.get("KITTY_B200_LIB", Path(__file__).resolve().parent.parent / LIB_NAME))
 
@@ -51,6 +51,13 @@ class KeyDequantArgs(ctypes.Structure):
                 ("boost_idx", c_ptr), ("bidx_s_head", c_i64), ("out", c_ptr), ("out_off", c_ptr),
                 ("out_s_ch", c_i64), ("out_s_tok", c_i64), ("n_jobs", c_i32), ("num_heads", c_i32),
                 ("head_dim", c_i32), ("group", c_i32), ("d_boost", c_i32), ("dtype", c_i32)]
+
+
+class ValueDequantArgs(ctypes.Structure):
+    _fields_ = [("val_codes", c_ptr), ("val_scale", c_ptr), ("val_zero", c_ptr), ("codes_s_page", c_i64),
+                ("codes_s_head", c_i64), ("meta_s_page", c_i64), ("meta_s_head", c_i64), ("meta_s_tok", c_i64),
+                ("src_page", c_ptr), ("head", c_ptr), ("out", c_ptr), ("out_off", c_ptr), ("out_s_tok", c_i64),
+                ("out_s_ch", c_i64), ("n_jobs", c_i32), ("head_dim", c_i32), ("group", c_i32), ("dtype", c_i32)]
 
 
 class DecodeArgs(ctypes.Structure):
@@ -96,6 +103,7 @@ SIGNATURES = {
     "kitty_quantize_key_pages": (ctypes.c_int, [ctypes.POINTER(KeyQuantArgs), c_ptr]),
     "kitty_quantize_value_pages": (ctypes.c_int, [ctypes.POINTER(ValueQuantArgs), c_ptr]),
     "kitty_dequantize_key_pages": (ctypes.c_int, [ctypes.POINTER(KeyDequantArgs), c_ptr]),
+    "kitty_dequantize_value_pages": (ctypes.c_int, [ctypes.POINTER(ValueDequantArgs), c_ptr]),
     "kitty_paged_decode_workspace_size": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), ctypes.POINTER(c_size),
                                                          ctypes.POINTER(c_i32)]),
     "kitty_paged_decode": (ctypes.c_int, [ctypes.POINTER(DecodeArgs), c_ptr]),
@@ -108,7 +116,8 @@ SIGNATURES = {
     "kitty_cache_prefill": (ctypes.c_int, [ctypes.POINTER(CacheState), ctypes.POINTER(PrefillArgs), c_ptr]),
     "kitty_cache_release": (ctypes.c_int, [ctypes.POINTER(CacheState), c_i32, c_ptr, c_ptr]),
 }
-STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs, 4: CacheState, 5: PrefillArgs}
+STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs, 4: CacheState, 5: PrefillArgs,
+           6: ValueDequantArgs}
 
 _lib: Optional[ctypes.CDLL] = None
 _lock = threading.Lock()
@@ -185,6 +194,18 @@ def dtype_code(dtype: torch.dtype) -> int:
 
 
 DTYPE_BF16_F16META = 3
+DTYPE_F16_F32OUT, DTYPE_BF16_F32OUT = 4, 5
+
+
+def dequant_dtype_code(meta: torch.dtype, out: torch.dtype) -> int:
+    """KITTY_DTYPE_* of a dequantiser call: metadata of a 16-bit type and an output of
+    the same type or float32."""
+    code = dtype_code(meta)
+    if out == meta:
+        return code
+    if out == torch.float32:
+        return DTYPE_F16_F32OUT if code == DTYPE_F16 else DTYPE_BF16_F32OUT
+    raise RuntimeError(f"output dtype {out} does not go with {meta} metadata (same type or float32)")
 
 
 def quant_dtype_code(src: torch.dtype, meta: torch.dtype) -> int:

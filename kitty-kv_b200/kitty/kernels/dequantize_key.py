@@ -20,8 +20,8 @@ def _launch(tensor_2bits, tensor_high_2bits, scale, zero_point, boost_idx, D_boo
     for t, n in ((tensor_2bits, "tensor_2bits"), (tensor_high_2bits, "tensor_high_2bits")):
         if not t.is_contiguous():
             raise RuntimeError(f"{n} must be contiguous")
-    if not (scale.dtype == zero_point.dtype == out.dtype) or out.dtype not in (torch.float16, torch.bfloat16):
-        raise RuntimeError("scale, zero_point and out must all be float16 or all bfloat16")
+    if scale.dtype != zero_point.dtype or scale.dtype not in (torch.float16, torch.bfloat16):
+        raise RuntimeError("scale and zero_point must both be float16 or both bfloat16")
     if scale.stride(0) != 1 or zero_point.stride(0) != 1 or boost_idx.stride(0) != 1:
         raise RuntimeError("scale, zero_point and boost_idx need unit stride")
     a = _lib.KeyDequantArgs()
@@ -34,7 +34,7 @@ def _launch(tensor_2bits, tensor_high_2bits, scale, zero_point, boost_idx, D_boo
     a.out = out.data_ptr(); a.out_off = _lib.zeros_const(dev, torch.int64).data_ptr()
     a.out_s_ch, a.out_s_tok = out.stride(0), out.stride(1)
     a.n_jobs, a.num_heads, a.head_dim, a.group, a.d_boost = 1, 1, D, G4 * 4, int(D_boost)
-    a.dtype = _lib.dtype_code(out.dtype)
+    a.dtype = _lib.dequant_dtype_code(scale.dtype, out.dtype)
     lib = _lib.load()
     _lib.check(lib.kitty_dequantize_key_pages(a, _lib.stream_ptr(dev)), "kitty_dequantize_key_pages")
 
@@ -53,19 +53,10 @@ def dequantize_key_page(tensor_2bits: torch.Tensor, tensor_high_2bits: torch.Ten
 def dequantize_key_page_torch(tensor_2bits: torch.Tensor, tensor_high_2bits: torch.Tensor, scale: torch.Tensor,
                               zero_point: torch.Tensor, boost_idx: torch.Tensor, D_boost: int) -> torch.Tensor:
     """Functional form returning the float32 (D, G) block, as the reference does
-    (``dequantize_key.py:95-97``).  A float32 result cannot come from the fp16
-    kernel without rounding, so this debug helper unpacks with torch
-    elementwise ops on the GPU (CUDA tensors only)."""
+    (``dequantize_key.py:35-97``), by the CUDA key dequantiser with float32 output."""
     D, G4 = tensor_2bits.shape
     dev = _lib.require_cuda(tensor_2bits, tensor_high_2bits, scale, zero_point, boost_idx)
-    shifts = torch.tensor([0, 2, 4, 6], dtype=torch.uint8, device=dev)
-    low = ((tensor_2bits.unsqueeze(-1) >> shifts) & 3).reshape(D, G4 * 4).to(torch.int32)
-    hi = torch.zeros_like(low)
-    if D_boost > 0:
-        bidx = boost_idx.to(torch.int64)
-        boosted = bidx < D_boost
-        rows = torch.where(boosted, bidx, torch.zeros_like(bidx))
-        hall = ((tensor_high_2bits.unsqueeze(-1) >> shifts) & 3).reshape(D_boost, G4 * 4).to(torch.int32)
-        hi = torch.where(boosted.unsqueeze(1), hall[rows], hi)
-    code = (low | (hi << 2)).float()
-    return (code - zero_point.float().unsqueeze(1)) * scale.float().unsqueeze(1)
+    out = torch.empty(D, G4 * 4, dtype=torch.float32, device=dev)
+    _launch(tensor_2bits, tensor_high_2bits, scale.contiguous(), zero_point.contiguous(), boost_idx.contiguous(),
+            D_boost, out)
+    return out

@@ -104,13 +104,34 @@ def quantize_value_page(value: torch.Tensor, out_packed: torch.Tensor, out_scale
     out_packed.copy_(codes); out_scale.copy_(scale); out_zero.copy_(zero)
 
 
-def _unpack_2bit(packed: torch.Tensor) -> torch.Tensor:
-    shifts = torch.tensor([0, 2, 4, 6], dtype=torch.uint8, device=packed.device)
-    return ((packed.unsqueeze(-1) >> shifts) & 3).reshape(*packed.shape[:-1], packed.shape[-1] * 4)
-
-
 def dequantize_value_page_torch(packed: torch.Tensor, scale: torch.Tensor, zero_point: torch.Tensor) -> torch.Tensor:
-    """(code - zp) * scale in float32, shape (G, D) (reference ``quantize_value.py:97-133``)."""
-    _lib.require_cuda(packed, scale, zero_point)
-    codes = _unpack_2bit(packed).float()
-    return (codes - zero_point.float().unsqueeze(1)) * scale.float().unsqueeze(1)
+    """(code - zp) * scale in float32, shape (G, D) (reference ``quantize_value.py:97-133``),
+    by the CUDA value dequantiser (``kitty_dequantize_value_pages``, float32 output).
+    ``scale`` / ``zero_point`` are (G,) float16 or bfloat16, any stride (the stride-2
+    views of the value metadata pool included)."""
+    dev = _lib.require_cuda(packed, scale, zero_point)
+    if packed.dtype != torch.uint8 or packed.dim() != 2:
+        raise RuntimeError("packed must be a (G, D/4) uint8 tensor")
+    G, D4 = packed.shape
+    if scale.numel() != G or zero_point.numel() != G or scale.dim() != 1 or zero_point.dim() != 1:
+        raise RuntimeError(f"scale and zero_point must be ({G},) vectors")
+    if scale.dtype != zero_point.dtype:
+        raise RuntimeError("scale and zero_point must have the same dtype")
+    if scale.stride(0) != zero_point.stride(0):
+        scale, zero_point = scale.contiguous(), zero_point.contiguous()
+    if not packed.is_contiguous():
+        packed = packed.contiguous()
+    out = torch.empty(G, D4 * 4, dtype=torch.float32, device=dev)
+    a = _lib.ValueDequantArgs()
+    a.val_codes = packed.data_ptr()
+    a.val_scale, a.val_zero = scale.data_ptr(), zero_point.data_ptr()
+    a.codes_s_page = a.codes_s_head = a.meta_s_page = a.meta_s_head = 0
+    a.meta_s_tok = scale.stride(0)
+    z32 = _lib.zeros_const(dev, torch.int32)
+    a.src_page = z32.data_ptr(); a.head = z32.data_ptr()
+    a.out, a.out_off = out.data_ptr(), _lib.zeros_const(dev, torch.int64).data_ptr()
+    a.out_s_tok, a.out_s_ch = out.stride(0), out.stride(1)
+    a.n_jobs, a.head_dim, a.group = 1, D4 * 4, G
+    a.dtype = _lib.dequant_dtype_code(scale.dtype, torch.float32)
+    _lib.check(_lib.load().kitty_dequantize_value_pages(a, _lib.stream_ptr(dev)), "kitty_dequantize_value_pages")
+    return out

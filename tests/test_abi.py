@@ -67,13 +67,15 @@ typedef int (*any_fn)(void);
 int main(void) {
   any_fn fns[] = {
     (any_fn)kitty_quantize_key_pages, (any_fn)kitty_quantize_value_pages, (any_fn)kitty_dequantize_key_pages,
+    (any_fn)kitty_dequantize_value_pages,
     (any_fn)kitty_paged_decode_workspace_size, (any_fn)kitty_paged_decode, (any_fn)kitty_paged_decode_noalloc,
     (any_fn)kitty_device_error_flags, (any_fn)kitty_decode_force_variant, (any_fn)kitty_cache_reset,
     (any_fn)kitty_cache_append, (any_fn)kitty_cache_prefill, (any_fn)kitty_cache_release};
   if (kitty_abi_version() != KITTY_ABI_VERSION) return 1;
   if (kitty_args_size(0) != sizeof(KittyKeyQuantArgs) || kitty_args_size(1) != sizeof(KittyValueQuantArgs) ||
       kitty_args_size(2) != sizeof(KittyKeyDequantArgs) || kitty_args_size(3) != sizeof(KittyDecodeArgs) ||
-      kitty_args_size(4) != sizeof(KittyCacheState) || kitty_args_size(5) != sizeof(KittyPrefillArgs))
+      kitty_args_size(4) != sizeof(KittyCacheState) || kitty_args_size(5) != sizeof(KittyPrefillArgs) ||
+      kitty_args_size(6) != sizeof(KittyValueDequantArgs))
     return 2;
   KittyDecodeArgs a;
   memset(&a, 0, sizeof(a));

@@ -70,3 +70,58 @@ def test_reference_arm_runs_on_cpu():
     line = json.loads(r.stdout.strip().splitlines()[-1])
     assert line["impl"] == "reference" and line["value"] > 0 and line["cpu_baseline"]["kind"] == "port"
     assert line["e2e"]["h2d_bytes_per_step"] == 0
+
+
+def _cpu_workload():
+    """A small decode workload in the shape bench.build_decode_workload returns, on CPU
+    tensors, with pools quantised by the oracle (permuted physical pages, ragged tails)."""
+    import numpy as np
+    import torch
+    from kitty import synthetic
+    from oracle import kitty_oracle as O
+    case = synthetic.make_decode_case(3, 3, 16, 4, 128, [32 + 5 * 128 + 7, 32 + 2 * 128, 32 + 3 * 128 + 100],
+                                      tails=[7, 0, 100])
+    H, D, G, K = case.num_kv_heads, case.head_dim, case.group, case.d_boost
+    total = sum(s.n_pages for s in case.seqs)
+    perm = np.random.default_rng(5).permutation(total + 2)[:total]
+    pools = [np.zeros((total + 2, H, D, G // 4), np.uint8), np.zeros((total + 2, H, K, G // 4), np.uint8),
+             np.zeros((total + 2, H, 2, D), np.float16), np.zeros((total + 2, H, G, D // 4), np.uint8),
+             np.zeros((total + 2, H, G, 2), np.float16)]
+    bt = np.zeros((3, 5), np.int32)
+    at = 0
+    for b, s in enumerate(case.seqs):
+        low, high, sc, zp = O.quantize_key_pages(s.page_keys(), case.boost_idx, K, case.sentinel)
+        codes, vs, vz = O.quantize_value_pages(s.page_values())
+        ids = perm[at:at + s.n_pages]
+        pools[0][ids], pools[1][ids] = low, high
+        pools[2][ids] = np.stack([sc, zp], axis=2)
+        pools[3][ids], pools[4][ids] = codes, np.stack([vs, vz], axis=3)
+        bt[b, :s.n_pages] = ids
+        at += s.n_pages
+    sk = np.stack([s.sink_kv()[0] for s in case.seqs]); sv = np.stack([s.sink_kv()[1] for s in case.seqs])
+    tk = np.zeros((3, H, 100, D), np.float16); tv = np.zeros_like(tk)
+    for b, s in enumerate(case.seqs):
+        a, c = s.tail_kv(); tk[b, :, :s.tail] = a; tv[b, :, :s.tail] = c
+    T = torch.from_numpy
+    w = dict(q=T(case.q), bt=T(bt), pools=[T(p) for p in pools], bidx=T(case.boost_idx), K=K, sink_k=T(sk),
+             sink_v=T(sv), tail_k=T(tk), tail_v=T(tv), tail_len=T(np.array([7, 0, 100], np.int32)),
+             layout=[(s.n_pages, s.tail) for s in case.seqs], H=H, Hq=case.num_q_heads, D=D)
+    sl = np.full(3, 32, np.int32)
+    exp = O.paged_attention_batched(case.q, bt, np.array([s.n_pages for s in case.seqs]), tuple(pools),
+                                    case.boost_idx, K, sk, sv, sl, tk, tv, np.array([7, 0, 100]))
+    return w, exp
+
+
+def test_oracle_check_accepts_the_oracle_and_flags_an_error():
+    import numpy as np
+    import torch
+    w, exp = _cpu_workload()
+    assert bench.oracle_sample(w["layout"]) == [0, 1]     # first = most pages, fewest pages
+    rows = [0, 1, 2]
+    ratio, abs_err = bench.oracle_check(w, torch.from_numpy(exp), rows)
+    assert ratio == 0.0 and abs_err == 0.0
+    bad = exp.copy()
+    bad[2, 13, 77] += np.float16(0.05)          # one element of the last KV head of row 2
+    ratio, abs_err = bench.oracle_check(w, torch.from_numpy(bad), rows)
+    assert ratio > 1.0 and abs_err > 0.04
+    assert bench.oracle_sample([(255, 96)] * 32) == [0, 31]

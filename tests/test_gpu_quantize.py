@@ -206,3 +206,57 @@ def test_random_shapes_match_oracle(shape):
         np.testing.assert_array_equal(got[0].cpu().numpy(), exp[0])
         np.testing.assert_array_equal(meta_by_value(got[1].cpu().numpy()), meta_by_value(exp[1]))
         np.testing.assert_array_equal(meta_by_value(got[2].cpu().numpy()), meta_by_value(exp[2]))
+
+
+@pytest.mark.parametrize("name", VALUE_CASES)
+def test_value_dequant_functional_vs_reference(golden_npz, name):
+    """dequantize_value_page_torch (reference quantize_value.py:97-133) on the CUDA value
+    dequantiser: float32 (G, D) equal bit for bit to the reference's recorded output,
+    from contiguous metadata and from the stride-2 views of a value_metadata pool."""
+    p = f"value/{name}/"
+    codes, sc, zp, exp = (golden_npz[p + n] for n in ("codes", "scale", "zero", "dequant"))
+    got = KK.dequantize_value_page_torch(cuda(codes), cuda(sc), cuda(zp))
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32 and tuple(got.shape) == exp.shape
+    np.testing.assert_array_equal(got.cpu().numpy(), exp)
+    G = codes.shape[0]
+    vm = torch.zeros(3, G, 2, dtype=torch.float16, device=DEV)
+    vm[1, :, 0] = cuda(sc); vm[1, :, 1] = cuda(zp)
+    got = KK.dequantize_value_page_torch(cuda(codes), vm[1, :, 0], vm[1, :, 1])
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(got.cpu().numpy(), exp)
+
+
+@pytest.mark.parametrize("name", KEY_CASES)
+def test_key_dequant_functional_vs_reference(golden_npz, name):
+    """dequantize_key_page_torch (reference dequantize_key.py:35-97) on the CUDA key
+    dequantiser with float32 output: equal bit for bit to the reference's recorded output."""
+    p = f"key/{name}/"
+    K = int(golden_npz[p + "params"][0])
+    got = KK.dequantize_key_page_torch(cuda(golden_npz[p + "low"]), cuda(golden_npz[p + "high"]),
+                                       cuda(golden_npz[p + "scale"]), cuda(golden_npz[p + "zero"]),
+                                       cuda(golden_npz[p + "boost_idx"]), K)
+    torch.cuda.synchronize()
+    assert got.dtype == torch.float32
+    np.testing.assert_array_equal(got.cpu().numpy(), golden_npz[p + "dequant"])
+
+
+@pytest.mark.parametrize("kind", ["bf16key", "bf16value"])
+def test_dequant_functional_bf16_metadata_vs_reference(golden_npz, kind):
+    """The same functional forms over bfloat16 metadata (a bfloat16 cache): float32 equal
+    to the reference's recorded output for every recorded page."""
+    names = sorted({k.split("/")[1] for k in golden_npz if k.startswith(kind + "/")})
+    assert names
+    for name in names:
+        p = f"{kind}/{name}/"
+        bf = lambda a: cuda(a.astype(np.float32)).to(torch.bfloat16)
+        if kind == "bf16key":
+            K = int(golden_npz[p + "params"][0])
+            got = KK.dequantize_key_page_torch(cuda(golden_npz[p + "low"]), cuda(golden_npz[p + "high"]),
+                                               bf(golden_npz[p + "scale"]), bf(golden_npz[p + "zero"]),
+                                               cuda(golden_npz[p + "boost_idx"]), K)
+        else:
+            got = KK.dequantize_value_page_torch(cuda(golden_npz[p + "codes"]), bf(golden_npz[p + "scale"]),
+                                                 bf(golden_npz[p + "zero"]))
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(got.cpu().numpy(), golden_npz[p + "dequant"], err_msg=p)

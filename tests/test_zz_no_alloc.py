@@ -7,8 +7,10 @@ array inside the library instead of a caller-provided workspace.
 Both entry points are called directly through the C ABI with the same argument
 struct; the allocation-free one must agree with kitty_paged_decode (fp16
 tolerance: atol 2e-3, rtol 1e-2) on two calls in a row, the second with other
-queries, so stale contents of the shared static array cannot leak into a result.
-This file is collected last on purpose."""
+queries, so stale contents of the shared static array cannot leak into a result,
+and with the numpy oracle on the same pools.  A batch whose partials at the
+library's default split count exceed the static array checks that the split count
+is lowered to fit.  This file is collected last on purpose."""
 
 from __future__ import annotations
 
@@ -26,8 +28,8 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 
-def _case_tensors(seed):
-    case = synthetic.make_decode_case(seed, 3, 32, 8, 128, [32 + 40 * 128 + 77, 32 + 9 * 128 + 5, 32 + 23 * 128])
+def _case_tensors(seed, contexts=(32 + 40 * 128 + 77, 32 + 9 * 128 + 5, 32 + 23 * 128)):
+    case = synthetic.make_decode_case(seed, len(contexts), 32, 8, 128, list(contexts))
     H, D, G, K = case.num_kv_heads, case.head_dim, case.group, case.d_boost
     n_phys = sum(s.n_pages for s in case.seqs)
     pools = [torch.zeros(n_phys, H, D, G // 4, dtype=torch.uint8, device=DEV),
@@ -39,9 +41,10 @@ def _case_tensors(seed):
     bidx = torch.from_numpy(case.boost_idx).to(DEV)
     B = len(case.seqs)
     W = max(s.n_pages for s in case.seqs)
+    assert B <= 64
     bt = torch.zeros(B, W, dtype=torch.int32, device=DEV)
     at = 0
-    S, Q = 32, max(s.tail for s in case.seqs)
+    S, Q = 32, max(max(s.tail for s in case.seqs), 1)
     sk = torch.zeros(B, H, S, D, dtype=torch.float16, device=DEV); sv = torch.zeros_like(sk)
     tk = torch.zeros(B, H, Q, D, dtype=torch.float16, device=DEV); tv = torch.zeros_like(tk)
     for b, s in enumerate(case.seqs):
@@ -105,6 +108,47 @@ def test_noalloc_decode_matches_workspace_decode_twice():
         torch.cuda.synchronize()
         assert torch.isfinite(got).all(), f"call {call}: output not fully written"
         np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), atol=2e-3, rtol=1e-2)
+        _assert_oracle(case, pools, bt, q, got, rows=range(3))
+
+
+def _assert_oracle(case, pools, bt, q, got, rows):
+    """The allocation-free output against the numpy oracle on the same pools."""
+    from oracle import kitty_oracle as O
+    np_pools = [p.cpu().numpy() for p in pools]
+    H, D = case.num_kv_heads, case.head_dim
+    for b in rows:
+        s = case.seqs[b]
+        sk, sv = s.sink_kv()
+        tk, tv = s.tail_kv()
+        exp = O.paged_attention(q[b].cpu().numpy(), bt[b, :s.n_pages].cpu().numpy(), *np_pools, case.boost_idx,
+                                case.d_boost, sk, sv, tk, tv, case.num_q_heads, H, D)
+        np.testing.assert_allclose(got[b].float().cpu().numpy(), exp.astype(np.float32), atol=2e-3, rtol=1e-2)
+
+
+def test_noalloc_lowers_the_split_count_to_fit():
+    """64 sequences x 8 KV heads with 2 pages each: at the library's default split
+    count the partials need more than the 8 MiB static array, so the entry point must
+    pick a smaller split count itself and still produce the right output."""
+    lib = _lib.load()
+    stream = torch.cuda.current_stream(torch.device(DEV)).cuda_stream
+    ctx = [32 + 2 * 128 + (i * 37) % 128 for i in range(64)]
+    case, pools, bidx, bt, npg, sk, sv, tk, tv, tl = _case_tensors(19, ctx)
+    q = torch.from_numpy(np.random.default_rng(5).standard_normal((64, 32, 128)).astype(np.float16)).to(DEV)
+    ref = torch.empty_like(q)
+    got = torch.full_like(q, float("nan"))
+    a = _args(case, pools, bidx, bt, npg, sk, sv, tk, tv, tl, q, ref)
+    need = _lib.c_size(0)
+    _lib.check(lib.kitty_paged_decode_workspace_size(a, need, None), "workspace_size")
+    assert need.value > 8 << 20, f"the case must overflow the static array at the default split count ({need.value})"
+    ws = torch.empty(need.value, dtype=torch.uint8, device=DEV)
+    a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel()
+    _lib.check(lib.kitty_paged_decode(a, stream), "kitty_paged_decode")
+    b = _args(case, pools, bidx, bt, npg, sk, sv, tk, tv, tl, q, got)
+    _lib.check(lib.kitty_paged_decode_noalloc(b, stream), "kitty_paged_decode_noalloc")
+    torch.cuda.synchronize()
+    assert torch.isfinite(got).all()
+    np.testing.assert_allclose(got.float().cpu().numpy(), ref.float().cpu().numpy(), atol=2e-3, rtol=1e-2)
+    _assert_oracle(case, pools, bt, q, got, rows=[0, 31, 63])
 
 
 def test_noalloc_rejects_explicit_splits_beyond_the_scratch():
@@ -114,7 +158,8 @@ def test_noalloc_rejects_explicit_splits_beyond_the_scratch():
     q = torch.zeros(3, 32, 128, dtype=torch.float16, device=DEV)
     out = torch.empty_like(q)
     a = _args(case, pools, bidx, bt, npg, sk, sv, tk, tv, tl, q, out)
-    # partials for ~2^19 splits of 3 x 32 query heads x 130 floats are far beyond 8 MiB
+    # the plan clamps the request to 1023 split slots (plus one), whose partials for
+    # 3 sequences x 32 query heads x 130 floats (about 50 MB) are far beyond 8 MiB
     a.num_splits = 1 << 20
     a.max_pages_per_seq = 1 << 20
     rc = lib.kitty_paged_decode_noalloc(a, stream)
