@@ -6,9 +6,13 @@ tests (tests/test_layout.py, tests/test_attention.py, tests/test_quantize.py).""
 
 from __future__ import annotations
 
+import json
+from pathlib import Path
+
 import numpy as np
 import pytest
 import torch
+import torch.nn as nn
 
 import kitty
 from kitty import pipeline as pipeline_mod
@@ -316,3 +320,81 @@ def test_bulk_push_reference_mode_goes_token_by_token(recorder):
     p.push_tokens(0, torch.arange(n, dtype=torch.float16).view(1, n, 1).expand(H, n, D),
                   (1000 + torch.arange(n, dtype=torch.float16)).view(1, n, 1).expand(H, n, D))
     assert len(recorder.key_calls) == 2 and [cl["n_valid"] for cl in recorder.value_calls] == [0, c.q_buffer_size]
+
+
+class _Attn(nn.Module):
+    def __init__(self, dm, H, D):
+        super().__init__()
+        self.q_proj = nn.Linear(dm, 2 * H * D, bias=False)
+        self.k_proj = nn.Linear(dm, H * D, bias=False)
+
+
+class _Block(nn.Module):
+    def __init__(self, dm, H, D):
+        super().__init__()
+        self.self_attn = _Attn(dm, H, D)
+        self.mlp = nn.Linear(dm, dm)
+
+    def forward(self, x):
+        self.self_attn.k_proj(x)
+        return x + self.mlp(x)
+
+
+class _ToyModel(nn.Module):
+    def __init__(self, L, dm, H, D):
+        super().__init__()
+        self.embed = nn.ModuleList([nn.Linear(dm, dm)])       # a ModuleList without k_proj comes first
+        self.layers = nn.ModuleList([_Block(dm, H, D) for _ in range(L)])
+
+    def forward(self, x):
+        for blk in self.layers:
+            x = blk(x)
+        return x
+
+
+def test_profiler_hooks_find_the_key_projections_and_rank_them():
+    """register_hooks locates layer i's k_proj by walking the model, the hooks see every
+    calibration token, and compute() applies the rank rule to mean |K| of the projection
+    outputs (checked against the oracle's rule on the same outputs); save / load round
+    trip the four files."""
+    import tempfile
+    torch.manual_seed(0)
+    L, dm, H, D = 3, 24, 2, 16
+    c = KittyConfig(num_layers=L, num_kv_heads=H, head_dim=D, boost_rate=0.25, device="cpu")
+    model = _ToyModel(L, dm, H, D)
+    xs = [torch.randn(2, 7, dm), torch.randn(1, 5, dm)]
+    outs = {0: [], 2: []}
+    with torch.no_grad():
+        for x in xs:                              # the inputs each layer's k_proj sees in forward
+            for i, blk in enumerate(model.layers):
+                if i in outs:
+                    outs[i].append(blk.self_attn.k_proj(x).reshape(-1, H, D))
+                x = x + blk.mlp(x)
+    prof = KittySensitivityProfiler(c, model)
+    prof.register_hooks([0, 2])
+    with torch.no_grad():
+        for x in xs:
+            model(x)
+    prof.remove_hooks()
+    with torch.no_grad():
+        model(xs[0])                              # hooks removed: no more tokens counted
+    assert prof._accumulators[0].token_count == 2 * 7 + 5
+    prof.compute()
+    for i in (0, 2):
+        k = torch.cat(outs[i]).abs().double().mean(dim=0).float().numpy()
+        np.testing.assert_array_equal(prof.boost_idx_uint8[i].numpy(), O.boost_idx_from_scores(k, c.d_boost,
+                                                                                              c.sentinel))
+    assert (prof.boost_idx_uint8[1] == torch.tensor([0, 1, 2, 3] + [c.sentinel] * (D - 4),
+                                                    dtype=torch.uint8)).all()   # no data: channel order
+    assert prof.boost_masks.sum().item() == L * H * c.d_boost
+    with tempfile.TemporaryDirectory() as d:
+        prof.save(d)
+        back = KittySensitivityProfiler.load(d, c)
+        assert torch.equal(back.boost_idx_uint8, prof.boost_idx_uint8) and torch.equal(back.scores_, prof.scores_)
+        assert json.loads((Path(d) / "meta.json").read_text())["token_count"] == {"0": 19, "2": 19}
+    with pytest.raises(RuntimeError, match="key_proj_getter"):
+        KittySensitivityProfiler(c, nn.Sequential(nn.Linear(4, 4))).register_hooks([0])
+    custom = KittySensitivityProfiler(c, model)
+    custom.register_hooks([1], key_proj_getter=lambda m, i: m.layers[i].self_attn.k_proj)
+    model(xs[1])
+    assert custom._accumulators[1].token_count == 5
