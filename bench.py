@@ -1,7 +1,7 @@
 """Benchmark: fused quantized paged decode attention (and page quantisation) on B200.
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl kitty|reference]
-                    [--workload config1..config5] [--variant auto|simt|mma|int8]
+                    [--workload config1..config5] [--variant auto|simt|int8|tc]
 
 One step = one decode step of one layer for the whole batch (every sequence,
 every query head) over the quantised KV pools resident in HBM; for config3 one
@@ -55,7 +55,6 @@ METRIC = "quantized paged decode-attn HBM GB/s (% of peak) & tokens/s at 1/2/4/8
 # (`--batch 8`, 1/8 of the page-heads) and scaled by 8: its traffic is per page-head.
 MEASURED_TRAFFIC = {
     ("config2", "decode_i8_kernel"): 652_503_552 + 4_320_256,
-    ("config2", "decode_mma_kernel"): 652_734_720 + 5_091_328,
     ("config4", "decode_i8_kernel"): (641_750_016 + 4_122_624) * 8,
 }
 
@@ -885,13 +884,15 @@ def quantize_arm(args, spec, d, device, local):
     }
 
 
-def decode_kernel_name(variant, g, D, G):
-    """Kernel family a decode call runs (the library's choice for "auto")."""
-    if variant == "auto":
-        variant = "int8" if (D == 128 and G == 128 and g <= 8) else "simt"
-    elif variant == "mma" and not (D == 128 and G == 128 and g <= 8):
-        variant = "int8" if (D == 128 and G == 128 and g <= 8) else "simt"
-    return {"int8": "decode_i8_kernel", "mma": "decode_mma_kernel", "simt": "decode_simt_kernel"}[variant]
+def decode_kernel_name(variant, g, D, G, fp16_regions=True):
+    """Kernel family a decode call runs (the library's choice for "auto"; the tcgen05
+    family takes pages-only calls and falls back to the library's choice otherwise)."""
+    i8 = D == 128 and G == 128 and g <= 8
+    if variant == "tc" and i8 and not fp16_regions:
+        return "decode_tc_kernel"
+    if variant in ("auto", "tc", "int8"):
+        variant = "int8" if i8 else "simt"
+    return {"int8": "decode_i8_kernel", "simt": "decode_simt_kernel"}[variant]
 
 
 def main():
@@ -902,7 +903,7 @@ def main():
     ap.add_argument("--impl", choices=["kitty", "reference"], default="kitty")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--variant", choices=["auto", "simt", "mma", "int8"], default="auto",
+    ap.add_argument("--variant", choices=["auto", "simt", "int8", "tc"], default="auto",
                     help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128 "
                          "and up to 8 query heads per KV head, CUDA-core kernel otherwise)")
     ap.add_argument("--batch", type=int, default=0,

@@ -404,10 +404,12 @@ int kitty_device_error_flags(uint32_t* flags, int clear);
 
 /* Test and benchmark hook, no counterpart in the reference: pin the decode
  * kernel family used by later kitty_paged_decode / _workspace_size / _noalloc
- * calls of this process (-1 = library choice, 0 = CUDA-core, 1 = fp16
- * tensor-core, 2 = integer tensor-core).  A pinned family that does not
- * support a call's shape falls back to the library choice.  The previous
- * setting is stored in *previous when it is not NULL. */
+ * calls of this process (-1 = library choice, 0 = CUDA-core, 2 = integer
+ * mma.sync tensor-core, 3 = integer tcgen05 with tensor-memory accumulators,
+ * which takes calls without fp16 sink / tail tokens only; 1 is not a family).
+ * A pinned family that does not support a call's shape falls back to the
+ * library choice.  The previous setting is stored in *previous when it is not
+ * NULL. */
 int kitty_decode_force_variant(int variant, int* previous);
 
 #ifdef __cplusplus

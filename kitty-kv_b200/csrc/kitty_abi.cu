@@ -53,7 +53,7 @@ int validate_decode(const KittyDecodeArgs* a) {
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: dtype must be KITTY_DTYPE_F16 or KITTY_DTYPE_BF16");
   if (a->sink_len_all < 0 || a->tail_len_all < 0)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: negative region length");
-  if (!simt_supports(*a) && !mma_supports(*a))
+  if (!simt_supports(*a))
     return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: head_dim > 256 or more than 16 query heads per KV head");
   return KITTY_OK;
 }
@@ -61,11 +61,10 @@ int validate_decode(const KittyDecodeArgs* a) {
 // Fill plan.num_splits / pages_per_split / variant / grid (no workspace pointers).
 int choose_variant(const KittyDecodeArgs* a) {
   const int forced = g_forced_variant.load();
+  if (forced == 3 && tc_supports(*a)) return 3;
   if (forced == 2 && i8_supports(*a)) return 2;
-  if (forced == 1 && mma_supports(*a)) return 1;
   if (forced == 0) return 0;
   if (i8_supports(*a)) return 2;
-  if (mma_supports(*a)) return 1;
   return 0;
 }
 
@@ -74,12 +73,12 @@ void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
   plan->grid = 0;
   plan->ws_m = plan->ws_l = plan->ws_o = nullptr;
   plan->ws_count = nullptr;
-  if (plan->variant == 2) {
-    i8_plan(*a, device_sm_count(), plan);
+  if (plan->variant == 3) {
+    tc_plan(*a, device_sm_count(), plan);
     return;
   }
-  if (plan->variant == 1) {
-    mma_plan(*a, device_sm_count(), plan);
+  if (plan->variant == 2) {
+    i8_plan(*a, device_sm_count(), plan);
     return;
   }
   const int maxp = std::max(0, a->max_pages_per_seq);
@@ -88,8 +87,7 @@ void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
   if (a->num_splits > 0) {
     splits = a->num_splits;
   } else {
-    const int ctas_per_sm = plan->variant == 1 ? mma_ctas_per_sm() : 4;
-    const int64_t target = int64_t(device_sm_count()) * ctas_per_sm * 2;
+    const int64_t target = int64_t(device_sm_count()) * 4 * 2;
     splits = int(std::max<int64_t>(1, (target + units - 1) / std::max<int64_t>(units, 1)));
   }
   splits = std::max(1, std::min({splits, std::max(1, maxp), kMaxDecodeSlots}));
@@ -160,21 +158,21 @@ int kitty_dequantize_value_pages(const KittyValueDequantArgs* args, void* stream
 int kitty_device_error_flags(uint32_t* flags, int clear) {
   clear_error();
   if (!flags) return fail(KITTY_ERR_INVALID_ARGUMENT, "device_error_flags: flags is NULL");
-  uint32_t a = 0, b = 0, c = 0;
-  int rc = read_decode_error(&a, clear);
+  uint32_t b = 0, c = 0, d = 0;
+  int rc = read_decode_error_i8(&b, clear);
   if (rc != KITTY_OK) return rc;
-  rc = read_decode_error_i8(&b, clear);
+  rc = read_decode_error_tc(&d, clear);
   if (rc != KITTY_OK) return rc;
   rc = read_cache_error(&c, clear);
   if (rc != KITTY_OK) return rc;
-  *flags = a | b | c;
+  *flags = b | c | d;
   return KITTY_OK;
 }
 
 int kitty_decode_force_variant(int variant, int* previous) {
   clear_error();
-  if (variant < -1 || variant > 2)
-    return fail(KITTY_ERR_INVALID_ARGUMENT, "decode_force_variant: variant must be -1, 0, 1 or 2");
+  if (variant < -1 || variant > 3 || variant == 1)
+    return fail(KITTY_ERR_INVALID_ARGUMENT, "decode_force_variant: variant must be -1, 0, 2 or 3");
   const int old = g_forced_variant.exchange(variant);
   if (previous) *previous = old;
   return KITTY_OK;
@@ -216,8 +214,8 @@ int kitty_paged_decode(const KittyDecodeArgs* args, void* stream) {
     if (plan.variant >= 1) plan.ws_count = reinterpret_cast<int*>(w + 2 * up(n * 4) + up(n * args->head_dim * 4));
   }
   cudaStream_t s = as_stream(stream);
-  rc = plan.variant == 2   ? launch_decode_i8(*args, plan, s)
-       : plan.variant == 1 ? launch_decode_mma(*args, plan, s)
+  rc = plan.variant == 3   ? launch_decode_tc(*args, plan, s)
+       : plan.variant == 2 ? launch_decode_i8(*args, plan, s)
                            : launch_decode_simt(*args, plan, s);
   if (rc != KITTY_OK) return rc;
   if (plan.variant >= 1 || plan.num_splits > 1) rc = launch_decode_merge(*args, plan, s);

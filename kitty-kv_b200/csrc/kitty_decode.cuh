@@ -19,8 +19,8 @@ namespace kitty {
 struct DecodePlan {
   int num_splits;
   int pages_per_split;
-  int variant;        // 0 = CUDA-core (any shape), 1 = fp16 tensor-core (D = G = 128, g <= 8),
-                      // 2 = integer tensor-core (D = G = 128, g <= 4)
+  int variant;        // 0 = CUDA-core (any shape), 2 = integer mma.sync (D = G = 128, g <= 8),
+                      // 3 = integer tcgen05 / tensor memory (D = G = 128, g <= 8, pages only)
   int grid;           // tensor-core variant: CTAs of the persistent grid
   float* ws_m;        // [B][H][S][g] running max per split (natural log units)
   float* ws_l;        // [B][H][S][g] running sum per split
@@ -32,17 +32,16 @@ struct DecodePlan {
 constexpr int kMaxDecodeSlots = 1024;
 
 int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
-int launch_decode_mma(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 bool simt_supports(const KittyDecodeArgs& a);
-bool mma_supports(const KittyDecodeArgs& a);
-int mma_ctas_per_sm();
-void mma_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
-int read_decode_error(uint32_t* flags, int clear);
 int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 bool i8_supports(const KittyDecodeArgs& a);
 int i8_ctas_per_sm();
 void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
 int read_decode_error_i8(uint32_t* flags, int clear);
+int launch_decode_tc(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
+bool tc_supports(const KittyDecodeArgs& a);
+void tc_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
+int read_decode_error_tc(uint32_t* flags, int clear);
 
 }  // namespace kitty

@@ -1,13 +1,12 @@
 // Paged GQA decode attention with integer tensor-core contractions
-// (head_dim = group = 128, up to 4 query heads per KV head).
+// (head_dim = group = 128, up to 8 query heads per KV head).
 //
-// Work decomposition and data movement are those of the fp16 tensor-core
-// kernel (kitty_decode_mma.cu): segments (sequence, KV head) of items (item 0 =
-// fp16 sinks + tail, items 1..n = quantised pages), one contiguous slice of
-// items per warp, one partial result per touched segment, per-warp key and
+// Work decomposition: segments (sequence, KV head) of items (the fp16 sinks + tail
+// in up to four chunk items, then the quantised pages), one contiguous slice of
+// cost units per warp, one partial result per touched segment, per-warp key and
 // value buffers filled by 1-D bulk async copies on bounded mbarrier waits.
 //
-// What changes is the arithmetic of a page-head.  The 2-bit codes stay
+// Arithmetic of a page-head.  The 2-bit codes stay
 // integers: one AND per register extracts four codes into the bytes of an
 // 8-bit MMA operand (mma.sync.m16n8k32, u8 x u8 -> s32), and the other operand
 // carries the folded scales in fixed point:
@@ -67,8 +66,14 @@ using namespace dev;
 // the oldest CTA's warps won the issue slots and finished well before the youngest,
 // which then set the kernel's end (config 2: 1.5 % slower).  With 8 query heads (255
 // registers) 8 warps per SM, as two CTAs of four (7 % faster than one CTA of eight).
+#ifndef KITTY_I8_W1
+#define KITTY_I8_W1 12
+#endif
+#ifndef KITTY_I8_SPLIT1
+#define KITTY_I8_SPLIT1 0
+#endif
 template <int kQG>
-__host__ __device__ constexpr int warps_per_cta() { return kQG == 1 ? 12 : 4; }
+__host__ __device__ constexpr int warps_per_cta() { return kQG == 1 ? KITTY_I8_W1 : 4; }
 template <int kQG>
 __host__ __device__ constexpr int ctas_per_sm() { return kQG == 1 ? 1 : 2; }
 constexpr int kD = 128, kG = 128;
@@ -691,7 +696,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       // ---- scores (log2 domain): s[qg][4 k + i] <-> token 32 k + 4 g_ + i; tile 4 half + i
       // holds tokens 64 half + 4 g_ + i (row g_, k = 2 half) and + 32 (row g_ + 8)
       float s[kQG][16];
-      if constexpr (kQG == 1) {
+      if constexpr (kQG == 1 && !KITTY_I8_SPLIT1) {
       const float zq = zqg[0], cq = cqg[0];
       int acc1[8][4], acc2[8][4];
       // ---- baseline plane
@@ -743,16 +748,18 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       }
       } else {
         // two query groups, one 64-token half at a time
-        const uint8_t* kb1g[2] = {kb1, kb1 + 4 * kRow};
-        const uint8_t* kb2g[2] = {kb2, kb2 + 4 * kRow};
+        const uint8_t* kb1g[kQG];
+        const uint8_t* kb2g[kQG];
+#pragma unroll
+        for (int qg = 0; qg < kQG; ++qg) { kb1g[qg] = kb1 + 4 * qg * kRow; kb2g[qg] = kb2 + 4 * qg * kRow; }
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          int a1[2][4][4], a2[2][4][4];
+          int a1[kQG][4][4], a2[kQG][4][4];
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            uint32_t b1[2][2], b2[2][2];
+            uint32_t b1[kQG][2], b2[kQG][2];
 #pragma unroll
-            for (int qg = 0; qg < 2; ++qg) {
+            for (int qg = 0; qg < kQG; ++qg) {
               b1[qg][0] = lds32(kb1g[qg] + 32 * ks + 4 * q_);
               b1[qg][1] = lds32(kb1g[qg] + 32 * ks + 16 + 4 * q_);
               b2[qg][0] = ones_col ? 0x01010101u : lds32(kb2g[qg] + 32 * ks + 4 * q_);
@@ -767,7 +774,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
               const uint32_t c0 = (r[0] >> sh) & m, c1 = (r[1] >> sh) & m, c2 = (r[2] >> sh) & m,
                              c3 = (r[3] >> sh) & m;
 #pragma unroll
-              for (int qg = 0; qg < 2; ++qg) {
+              for (int qg = 0; qg < kQG; ++qg) {
                 if (ks == 0) {
                   mma_k32_z(a1[qg][i], c0, c1, c2, c3, b1[qg][0], b1[qg][1]);
                   mma_k32_z(a2[qg][i], c0, c1, c2, c3, b2[qg][0], b2[qg][1]);
@@ -781,21 +788,26 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           for (int bs = 0; bs < nb; bs += 16) {
             const uint4 e4 = *reinterpret_cast<const uint4*>(ent + bs + 4 * q_);
             const uint32_t es[4] = {e4.x, e4.y, e4.z, e4.w};
-            uint32_t r[4], bb1[2] = {0u, 0u}, bb2[2] = {0u, 0u};
+            uint32_t r[4], bb1[kQG], bb2[kQG];
+#pragma unroll
+            for (int qg = 0; qg < kQG; ++qg) bb1[qg] = bb2[qg] = 0u;
             ldsm_t_x2(smem_u32(kh) + (ent[bs + (lane & 15)] & 0xffffu) + 16u * (lane >> 4), r);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint32_t pos = es[kk] >> 16;
 #pragma unroll
-              for (int qg = 0; qg < 2; ++qg) {
+              for (int qg = 0; qg < kQG; ++qg) {
                 bb1[qg] |= uint32_t(kb1g[qg][pos]) << (8 * kk);
                 bb2[qg] |= uint32_t(kb2g[qg][pos]) << (8 * kk);
               }
             }
-            if (ones_col) bb2[0] = bb2[1] = 0x01010101u;
+            if (ones_col) {
+#pragma unroll
+              for (int qg = 0; qg < kQG; ++qg) bb2[qg] = 0x01010101u;
+            }
             const uint32_t x0 = r[2 * half], x1 = r[2 * half + 1];
 #pragma unroll
-            for (int qg = 0; qg < 2; ++qg) {
+            for (int qg = 0; qg < kQG; ++qg) {
               mma_k16(a1[qg][0], high_code<0>(x0), high_code<0>(x1), bb1[qg]);
               mma_k16(a2[qg][0], high_code<0>(x0), high_code<0>(x1), bb2[qg]);
               mma_k16(a1[qg][1], high_code<1>(x0), high_code<1>(x1), bb1[qg]);
@@ -807,7 +819,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
             }
           }
 #pragma unroll
-          for (int qg = 0; qg < 2; ++qg)
+          for (int qg = 0; qg < kQG; ++qg)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const float f = cqg[qg] * (i == 0 ? 1.0f : i == 1 ? 0.25f : 0.0625f);
@@ -821,7 +833,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
             }
         }
       }
-      if constexpr (kQG != 1) next_keys();
+      if constexpr (kQG != 1 || KITTY_I8_SPLIT1) next_keys();
 
       if (!mbar_wait(bar_v, v_phase)) { failed = true; break; }
       v_phase ^= 1u;
@@ -879,7 +891,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         }
         }
         __syncwarp();
-        if constexpr (kQG == 1) {
+        if constexpr (kQG == 1 && !KITTY_I8_SPLIT1) {
         const float dv = dvg[0];
         State& sto = st[0];
         // ---- values: M = channels, K = tokens 32 ks + k
@@ -902,15 +914,17 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
           sto.o[8 * half + 4 + i] = o.y;
         }
         } else {
-          const uint8_t* vbg[2] = {vb, vb + 4 * kRow};
+          const uint8_t* vbg[kQG];
+#pragma unroll
+          for (int qg = 0; qg < kQG; ++qg) vbg[qg] = vb + 4 * qg * kRow;
 #pragma unroll
           for (int half = 0; half < 2; ++half) {
-            int acc[2][4][4];
+            int acc[kQG][4][4];
 #pragma unroll
             for (int ks = 0; ks < 4; ++ks) {
-              uint32_t bv[2][2];
+              uint32_t bv[kQG][2];
 #pragma unroll
-              for (int qg = 0; qg < 2; ++qg) {
+              for (int qg = 0; qg < kQG; ++qg) {
                 bv[qg][0] = lds32(vbg[qg] + 32 * ks + 4 * q_);
                 bv[qg][1] = lds32(vbg[qg] + 32 * ks + 16 + 4 * q_);
               }
@@ -920,14 +934,14 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
               for (int i = 0; i < 4; ++i) {
                 const uint32_t m = 0x03030303u << (2 * i);
 #pragma unroll
-                for (int qg = 0; qg < 2; ++qg) {
+                for (int qg = 0; qg < kQG; ++qg) {
                   if (ks == 0) mma_k32_z(acc[qg][i], r[0] & m, r[1] & m, r[2] & m, r[3] & m, bv[qg][0], bv[qg][1]);
                   else mma_k32(acc[qg][i], r[0] & m, r[1] & m, r[2] & m, r[3] & m, bv[qg][0], bv[qg][1]);
                 }
               }
             }
 #pragma unroll
-            for (int qg = 0; qg < 2; ++qg)
+            for (int qg = 0; qg < kQG; ++qg)
 #pragma unroll
               for (int i = 0; i < 4; ++i) {
                 const float f = dvg[qg] * (i == 0 ? 1.0f : i == 1 ? 0.25f : i == 2 ? 0.0625f : 0.015625f);
@@ -1017,7 +1031,10 @@ int i8_warps(int qg) { return qg == 1 ? warps_per_cta<1>() : warps_per_cta<2>();
 int i8_ctas(int qg) { return qg == 1 ? ctas_per_sm<1>() : ctas_per_sm<2>(); }
 }  // namespace
 
-// Same slicing rule as the fp16 tensor-core variant (see mma_plan).
+// Slots per segment S = num_splits (default kSlotsTarget, more when there are fewer
+// segment cost units than warps need for a full grid): every warp takes at least
+// F_min = ceil(units_max / S) units, so a segment spans at most ceil(units_max / F_min)
+// + 1 warps, which is the slot count the merge reads.
 void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   // cost units of the longest segment: pages + weighted fp16 chunk items
   const int items_max = a.max_pages_per_seq + kFp16Weight * dev::kMaxFp16Items;

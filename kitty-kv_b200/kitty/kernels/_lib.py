@@ -172,11 +172,11 @@ CACHE_ERRORS = {1 << 1: "no free page", 1 << 2: "block table full",
                 1 << 3: "sequence id out of range or repeated in a batch", 1 << 4: "free-page stack overflow",
                 1 << 5: "prefill page budget (max_pages) too small"}
 
-DECODE_VARIANTS = {"auto": -1, "simt": 0, "mma": 1, "int8": 2}
+DECODE_VARIANTS = {"auto": -1, "simt": 0, "int8": 2, "tc": 3}
 
 
 def force_decode_variant(name: str) -> str:
-    """Pin the decode kernel family ("auto", "simt", "mma" or "int8") for later decode
+    """Pin the decode kernel family ("auto", "simt", "int8" or "tc") for later decode
     calls of this process; returns the previous setting.  Shapes the pinned family
     does not support fall back to the library's choice."""
     prev = ctypes.c_int(-1)

@@ -119,7 +119,7 @@ def test_empty_context_gives_zeros():
     assert torch.count_nonzero(out).item() == 0
 
 
-@pytest.fixture(params=["auto", "simt", "mma", "int8"])
+@pytest.fixture(params=["auto", "simt", "int8"])
 def variant(request):
     """Each decode kernel family pinned in turn (shapes a family does not support fall
     back to the library's choice)."""
@@ -196,3 +196,41 @@ def test_fp16_heavy_batches_vs_oracle(splits, variant):
     exp = O.paged_attention_batched(case.q, bt, npg, tuple(p.cpu().numpy() for p in pools), case.boost_idx,
                                     case.d_boost, sk, sv, sl, tk, tv, tl)
     assert_close(run_batched(case, pools, phys_of, num_splits=splits), exp)
+
+
+@pytest.mark.parametrize("hq,rate", [(32, 0.125), (64, 0.125), (32, 0.25), (24, 0.25), (8, 0.0)])
+def test_tcgen05_family_on_pages_only_batches(hq, rate):
+    """The tcgen05 family (integer MMAs with the operands and sums in tensor memory; it takes
+    calls without fp16 sink / tail tokens) against the oracle and the mma.sync integer
+    family on the same pools: 1, 4, 6 and 8 query heads per KV head, d_boost 0, 16 and 32,
+    permuted physical pages, ragged page counts, and an out-of-range block-table entry
+    (that page is skipped by every family)."""
+    H = 8
+    contexts = [32 + 40 * 128, 32 + 3 * 128, 32 + 17 * 128, 32 + 1 * 128]
+    case = synthetic.make_decode_case(300 + hq, len(contexts), hq, H, 128, contexts, boost_rate=rate,
+                                      tails=[0] * len(contexts))
+    total = sum(s.n_pages for s in case.seqs)
+    n_phys = total + 5
+    phys_of = GC.phys_layout(case, 301, n_phys)
+    pools = build_pools_gpu(case, phys_of, n_phys)
+    bt, npg = GC.block_table(case, phys_of)
+    bt[2, 5] = n_phys + 100          # out of range: skipped
+    outs = {}
+    for fam in ("tc", "int8"):
+        prev = KK._lib.force_decode_variant(fam)
+        try:
+            out = KK.paged_attention_batched(cuda(case.q), cuda(bt), cuda(npg), *pools, cuda(case.boost_idx),
+                                             case.d_boost, sink_len=0, tail_len=0)
+            torch.cuda.synchronize()
+        finally:
+            KK._lib.force_decode_variant(prev)
+        assert KK._lib.device_error_flags() == 0
+        outs[fam] = out.cpu().numpy()
+    np_pools = tuple(p.cpu().numpy() for p in pools)
+    H_, D = case.num_kv_heads, case.head_dim
+    z = np.zeros((H_, 0, D), np.float16)
+    for b, s in enumerate(case.seqs):
+        pages = [p for p in bt[b, :npg[b]] if p < n_phys]
+        exp = O.paged_attention(case.q[b], pages, *np_pools, case.boost_idx, case.d_boost, z, z, z, z, hq, H_, D)
+        assert_close(outs["tc"][b], exp)
+    assert_close(outs["tc"], outs["int8"])
