@@ -262,10 +262,11 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 
 // Merge the per-split partials: out = sum_s e^{m_s-M} o_s / sum_s e^{m_s-M} l_s.
 // Combines the split partials of one (sequence, query head): max M over the slots,
-// weights w_s = exp(m_s - M), L = sum_s w_s l_s, out = sum_s w_s o_s / L.  The slot
-// weights are computed once (one lane per slot) and kept in shared memory, and the
-// accumulation over slots issues its loads in groups of eight, so a call with many
-// slots costs a few memory latencies instead of one per slot.
+// weights w_s = exp(m_s - M), L = sum_s w_s l_s, out = sum_s w_s o_s / L.  Up to 32
+// slots (the usual case) each warp computes the weights itself, one lane per slot, and
+// broadcasts them by shuffles; with more slots the weights are computed once per block
+// and kept in shared memory, and the accumulation issues its loads in groups of eight,
+// so a call with many slots costs a few memory latencies instead of one per slot.
 constexpr int kMergeThreads = 128;
 constexpr int kMergeMaxSlots = kMaxDecodeSlots;
 
@@ -282,6 +283,41 @@ decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // slots written for this (sequence, head): all of them, or the recorded count
   const int nsl = min(plan.ws_count ? min(max(plan.ws_count[int64_t(b) * H + h], 0), plan.num_splits)
                                     : plan.num_splits, kMergeMaxSlots);
+  uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + qhg * a.out_s_head;
+  const float* o = plan.ws_o + ((base) * g + qh) * int64_t(D);
+  const int64_t slot_stride = int64_t(g) * D;
+  if (nsl <= 32) {
+    // few slots (the usual case): every warp derives the slot weights itself, lane s for
+    // slot s, and broadcasts them by shuffles - no block-wide reduction or barrier
+    const float ms = lane < nsl ? plan.ws_m[(base + lane) * g + qh] : -INFINITY;
+    float M = ms;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, d));
+    const float ws = (ms == -INFINITY) ? 0.f : __expf(ms - M);
+    float L = lane < nsl ? ws * plan.ws_l[(base + lane) * g + qh] : 0.f;
+#pragma unroll
+    for (int d = 16; d > 0; d >>= 1) L += __shfl_xor_sync(0xffffffffu, L, d);
+    // whole warps walk the channels (the shuffles need every lane), loads guarded by c < D
+    for (int c0 = warp * 32; c0 < D; c0 += kMergeThreads) {
+      const int c = c0 + lane;
+      const bool in = c < D;
+      float acc = 0.f;
+      int s = 0;
+      for (; s + 4 <= nsl; s += 4) {
+        float v[4];
+#pragma unroll
+        for (int k = 0; k < 4; ++k) v[k] = in ? o[(s + k) * slot_stride + c] : 0.f;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) acc += __shfl_sync(0xffffffffu, ws, s + k) * v[k];
+      }
+      for (; s < nsl; ++s) {
+        const float v = in ? o[s * slot_stride + c] : 0.f;
+        acc += __shfl_sync(0xffffffffu, ws, s) * v;
+      }
+      if (in) out[c] = f2h(L > 0.f ? acc / L : 0.f);
+    }
+    return;
+  }
   float mx = -INFINITY;
   for (int s = tid; s < nsl; s += kMergeThreads) mx = fmaxf(mx, plan.ws_m[(base + s) * g + qh]);
 #pragma unroll
@@ -314,9 +350,6 @@ decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   }
   __syncthreads();
   const float L = s_L;
-  uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + qhg * a.out_s_head;
-  const float* o = plan.ws_o + ((base) * g + qh) * int64_t(D);
-  const int64_t slot_stride = int64_t(g) * D;
   for (int c = tid; c < D; c += kMergeThreads) {
     float acc = 0.f;
     int s = 0;
