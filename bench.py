@@ -117,10 +117,12 @@ def sequence_layout(spec):
     return [(n, T - SINK - n * GROUP)] * B
 
 
-def decode_bytes(layout, Hq, H, D, G, K):
+def decode_bytes(layout, Hq, H, D, G, K, fp16_regions=True):
     """Bytes one decode step must move for these sequences (each page-head once, fp16
-    sinks and tails for keys and values, q and out, block-table entries)."""
-    return sum(H * (n * page_head_bytes(D, G, K) + (SINK + t) * D * 2 * 2) + 2 * Hq * D * 2 + 4 * n
+    sinks and tails for keys and values unless the step skips them, q and out,
+    block-table entries)."""
+    f = 1 if fp16_regions else 0
+    return sum(H * (n * page_head_bytes(D, G, K) + f * (SINK + t) * D * 2 * 2) + 2 * Hq * D * 2 + 4 * n
                for n, t in layout)
 
 
@@ -306,6 +308,10 @@ def build_decode_workload(spec, seq_ids, heads, device, seed):
 
 def decode_call(w, q=None, bt=None, npg=None, out=None):
     from kitty import kernels as KK
+    if w.get("pages_only"):   # the quantised pages alone (no fp16 sink / tail tokens)
+        return KK.paged_attention_batched(
+            w["q"] if q is None else q, w["bt"] if bt is None else bt, w["npg"] if npg is None else npg,
+            *w["pools"], w["bidx"], w["K"], sink_len=0, tail_len=0, out=out, max_pages_per_seq=w["n_pages"])
     return KK.paged_attention_batched(
         w["q"] if q is None else q, w["bt"] if bt is None else bt, w["npg"] if npg is None else npg, *w["pools"],
         w["bidx"], w["K"], sink_k=w["sink_k"], sink_v=w["sink_v"], sink_len=SINK, tail_k=w["tail_k"],
@@ -341,6 +347,7 @@ def oracle_check(w, out, rows):
     bidx = w["bidx"].cpu().numpy()
     tails = w["tail_len"]
     H, Hq, D = w["H"], w["Hq"], w["D"]
+    pages_only = bool(w.get("pages_only"))
     g = Hq // H
     jobs = []
     for i in rows:
@@ -351,6 +358,8 @@ def oracle_check(w, out, rows):
         q = w["q"][i].cpu().numpy()
         reg = [w["sink_k"][i].cpu().numpy(), w["sink_v"][i].cpu().numpy(),
                w["tail_k"][i, :, :t].cpu().numpy(), w["tail_v"][i, :, :t].cpu().numpy()]
+        if pages_only:
+            reg = [r[:, :0] for r in reg]
         got = out[i].float().cpu().numpy()
         for h in range(H):
             jobs.append((q[h * g:(h + 1) * g], [np.ascontiguousarray(p[:, h:h + 1]) for p in pools],
@@ -624,9 +633,10 @@ def decode_arm(args, spec, d, device, local):
     seq_ids, heads = shard(spec, world, rank)
     seed = 1234 + rank if replica else 1234
     w = build_decode_workload(spec, seq_ids, heads, device, seed)
+    w["pages_only"] = bool(spec.get("pages_only"))
     B, Hq, H, D, G, K = w["B"], w["Hq"], w["H"], w["D"], w["G"], w["K"]
-    kernel = decode_kernel_name(args.variant, Hq // max(H, 1), D, G)
-    nbytes_local = decode_bytes(w["layout"], Hq, H, D, G, K)
+    kernel = decode_kernel_name(args.variant, Hq // max(H, 1), D, G, fp16_regions=not w["pages_only"])
+    nbytes_local = decode_bytes(w["layout"], Hq, H, D, G, K, fp16_regions=not w["pages_only"])
     nbytes_total = nbytes_local * world if replica else d.reduce(nbytes_local, d.dist.ReduceOp.SUM)
     stream = torch.cuda.current_stream(device)
     gather = spec["shard"] == "kv_head" and world > 1
@@ -906,6 +916,9 @@ def main():
     ap.add_argument("--variant", choices=["auto", "simt", "int8", "tc"], default="auto",
                     help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128 "
                          "and up to 8 query heads per KV head, CUDA-core kernel otherwise)")
+    ap.add_argument("--pages-only", action="store_true",
+                    help="decode the quantised pages alone (no fp16 sink / tail tokens; the bytes count "
+                         "the pages only): isolates the page path, and the only calls the tcgen05 family takes")
     ap.add_argument("--batch", type=int, default=0,
                     help="override the workload's batch (smaller cases for profiler captures); the JSON "
                          "line's config then records the reduced batch")
@@ -916,6 +929,10 @@ def main():
         if spec["kind"] != "decode" or "batch" not in spec:
             raise SystemExit("--batch applies to the decode workloads with a fixed batch")
         spec["batch"] = args.batch
+    if args.pages_only:
+        if spec["kind"] != "decode":
+            raise SystemExit("--pages-only applies to the decode workloads")
+        spec["pages_only"] = True
     if args.impl == "reference":
         reference_arm(args, spec)
     else:
