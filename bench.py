@@ -920,14 +920,14 @@ def main():
                     help="decode the quantised pages alone (no fp16 sink / tail tokens; the bytes count "
                          "the pages only): isolates the page path, and the only calls the tcgen05 family takes")
     ap.add_argument("--batch", type=int, default=0,
-                    help="override the workload's batch (smaller cases for profiler captures); the JSON "
+                    help="override the workload's batch of sequences (smaller cases for profiler captures); the JSON "
                          "line's config then records the reduced batch")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
     spec = dict(WORKLOADS[args.workload])
     if args.batch > 0:
-        if spec["kind"] != "decode" or "batch" not in spec:
-            raise SystemExit("--batch applies to the decode workloads with a fixed batch")
+        if "batch" not in spec:
+            raise SystemExit("--batch applies to the workloads with a fixed batch")
         spec["batch"] = args.batch
     if args.pages_only:
         if spec["kind"] != "decode":

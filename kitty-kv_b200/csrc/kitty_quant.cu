@@ -15,9 +15,20 @@
 // D = G = 128 kernels keep the block in registers (see below).
 
 #include "kitty_common.cuh"
+#include "kitty_ptx.cuh"
 
 namespace kitty {
 namespace {
+
+using dev::fma2;
+using dev::prmt;
+
+#ifndef KITTY_Q_MINB
+#define KITTY_Q_MINB 4    // resident CTAs of the D = G = 128 quantisers the register budget is set for
+#endif
+#ifndef KITTY_Q_PAIRS
+#define KITTY_Q_PAIRS 1   // the fixed-point rounding on packed fp32 pairs (0: scalar FMAs)
+#endif
 
 constexpr int kQuantThreads = 256;
 
@@ -338,6 +349,31 @@ __device__ __forceinline__ void fast_pair(uint32_t hx, float2 r, float2 mz, floa
   c1 = __float_as_uint(fminf(fmaxf(f1, kMagic), top.y));
 }
 
+// Fast codes of an fp16 pair in one word: lane k (16 bits) = code of element k, clamped
+// to [0, maxq] as signed 16-bit integers.  Same rounding as fast_pair (fma(x, r, kMagic +
+// zp) = kMagic + zp + rint(x r), on fp32 pairs), one near-tie test for the pair (the
+// larger rounding distance; both elements are recomputed exactly when it is near a
+// half-integer).  Valid while |zp + rint(x r)| < 2^15: the caller routes channels whose
+// |x| / scale can reach 16000 (near-constant channels far from zero) to fast_pair.
+template <bool kBf16>
+__device__ __forceinline__ uint32_t fast_pair16(uint32_t hx, float2 r, float2 mz, uint32_t lim, bool& tie) {
+  const float2 x = Half16<kBf16>::to_f2(hx);
+#if KITTY_Q_PAIRS
+  const float2 f = fma2(x, r, mz);                               // kMagic + zp + rint(x r)
+  const float2 t = fma2(f, make_float2(-1.0f, -1.0f), mz);       // -rint(x r), exact
+  const float2 e = fma2(x, r, t);                                // x r - rint(x r)
+#else
+  const float2 f = make_float2(__fmaf_rn(x.x, r.x, mz.x), __fmaf_rn(x.y, r.y, mz.y));   // kMagic + zp + rint(x r)
+  const float2 e = make_float2(__fmaf_rn(x.x, r.x, mz.x - f.x), __fmaf_rn(x.y, r.y, mz.y - f.y));   // x r - rint(x r)
+#endif
+  tie |= fmaxf(fabsf(e.x), fabsf(e.y)) > kNearHalf;
+  uint32_t w, v;
+  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w) : "r"(__float_as_uint(f.x)), "r"(__float_as_uint(f.y)));
+  asm("max.s16x2 %0, %1, %2;" : "=r"(v) : "r"(w), "r"(0u));
+  asm("min.s16x2 %0, %1, %2;" : "=r"(w) : "r"(v), "r"(lim));
+  return w;
+}
+
 // Exact codes of the flagged elements of one 8-element row (bit j of `flags` =
 // element j; element j's fp16 value at src[j * stride]); patches the 2-bit fields
 // of lo (bits 0-1 of each code) and hi (bits 2-3).  Rare: kept out of line.
@@ -353,19 +389,6 @@ __device__ __noinline__ uint2 patch_row(uint32_t flags, const uint16_t* src, int
   return make_uint2(lo, hi);
 }
 
-// four codes (low bytes of c0..c3) -> bits 0-1 of each into one byte (code k at 2k)
-__device__ __forceinline__ uint32_t pack4(uint32_t c0, uint32_t c1, uint32_t c2, uint32_t c3, int shift) {
-  uint32_t w;
-  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(w) : "r"(c0), "r"(c1));
-  uint32_t w2;
-  asm("prmt.b32 %0, %1, %2, 0x0040;" : "=r"(w2) : "r"(c2), "r"(c3));
-  asm("prmt.b32 %0, %1, %2, 0x5410;" : "=r"(w) : "r"(w), "r"(w2));
-  w = (w >> shift) & 0x03030303u;
-  // x (2^24 + 2^18 + 2^12 + 2^6) puts b0 + 4 b1 + 16 b2 + 64 b3 in bits 24..31; the
-  // other partial products stay below 2^24 (at most 3 * 5525568) or wrap past 2^32
-  return (w * 0x01041040u) >> 24;
-}
-
 // low plane byte of channel c, token word j (tokens 4j..4j+3) in the swizzled
 // shared staging: 32-bit word (j / 4) ^ (c >> 3 & 7) of row c
 __device__ __forceinline__ int low_swz(int c, int byte) {
@@ -373,13 +396,14 @@ __device__ __forceinline__ int low_swz(int c, int byte) {
 }
 
 template <bool kBf16, bool kMetaBf16>
-__global__ void __launch_bounds__(kFastThreads, 4)
+__global__ void __launch_bounds__(kFastThreads, KITTY_Q_MINB)
 quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
   using T = Half16<kBf16>;
   constexpr int D = 128, G = 128, G4 = 32;
   __shared__ __align__(16) uint32_t s_red[8][64][2];   // per warp, per channel pair: (min, max) half2
   __shared__ float s_scale[D], s_zp[D], s_maxq[D], s_r[D];
   __shared__ int s_row[D];
+  __shared__ int s_wide[D];   // |x| / scale can reach 16000: the 16-bit lane path does not apply
   __shared__ int s_nonfinite;
   __shared__ __align__(16) uint8_t s_low[D * G4];
   __shared__ __align__(16) uint32_t s_high[128 * G4 / 4];
@@ -443,6 +467,7 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
     zp = tmin(tmax(zp, 0.0f), maxq);
     s_scale[c] = scale; s_zp[c] = zp; s_maxq[c] = maxq; s_r[c] = __frcp_rn(scale);
     s_row[c] = (boosted && r < K) ? r : -1;
+    s_wide[c] = !(fmaxf(fabsf(mnf), fabsf(mxf)) * __frcp_rn(scale) < 16000.0f);
     out_scale[c] = Half16<kMetaBf16>::meta(scale);
     out_zero[c] = Half16<kMetaBf16>::meta(zp);
     if (!(isfinite(mnf) && isfinite(mxf) && isfinite(scale))) s_nonfinite = 1;
@@ -460,31 +485,46 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
   };
   const uint16_t* my_src = src + (8 * tg) * a.key_s_tok + 8 * cg;   // this thread's tile (token-major)
   if (s_nonfinite == 0) {
-    uint32_t mlo = 0u, mhi = 0u;   // near-tie flags: channel k, token i -> bit 8 (k & 3) + i of mlo (k < 4) / mhi
 #pragma unroll
     for (int w = 0; w < 4; ++w) {
       const int c = 8 * cg + 2 * w;
       const float2 r = make_float2(s_r[c], s_r[c + 1]);
       const float2 mz = make_float2(kMagic + s_zp[c], kMagic + s_zp[c + 1]);
-      const float2 top = make_float2(kMagic + s_maxq[c], kMagic + s_maxq[c + 1]);
-      uint32_t ca[8], cb[8];
-      uint32_t& m = (w < 2) ? mlo : mhi;
-      const int kb = 8 * ((2 * w) & 3);
+      // code words of channels c, c + 1 (16-bit lanes) for tokens 8 tg + i, folded as they come
+      // into the low-plane (bits 0-1) and high-plane (bits 2-3) fields of tokens 0-3 / 4-7
+      uint32_t l03 = 0u, l47 = 0u, h03 = 0u, h47 = 0u;
+      uint32_t tie = 0u;
+      auto fold = [&](int i, uint32_t wv) {
+        const int sh = 2 * (i & 3);
+        const uint32_t lo = (wv & 0x00030003u) << sh, hi = ((wv >> 2) & 0x00030003u) << sh;
+        if (i < 4) { l03 += lo; h03 += hi; } else { l47 += lo; h47 += hi; }
+      };
+      if (!(s_wide[c] | s_wide[c + 1])) {
+        const uint32_t lim = uint32_t(s_maxq[c]) | (uint32_t(s_maxq[c + 1]) << 16);
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        fast_pair<kBf16>(word_of(t.row[i], w), r, mz, top, m, 1u << (kb + i), 1u << (kb + 8 + i), ca[i], cb[i]);
-      uint32_t lo_a = pack4(ca[0], ca[1], ca[2], ca[3], 0) | (pack4(ca[4], ca[5], ca[6], ca[7], 0) << 8);
-      uint32_t hi_a = pack4(ca[0], ca[1], ca[2], ca[3], 2) | (pack4(ca[4], ca[5], ca[6], ca[7], 2) << 8);
-      uint32_t lo_b = pack4(cb[0], cb[1], cb[2], cb[3], 0) | (pack4(cb[4], cb[5], cb[6], cb[7], 0) << 8);
-      uint32_t hi_b = pack4(cb[0], cb[1], cb[2], cb[3], 2) | (pack4(cb[4], cb[5], cb[6], cb[7], 2) << 8);
-      const uint32_t fa = (m >> kb) & 0xffu, fb = (m >> (kb + 8)) & 0xffu;
-      if (fa) {
-        const uint2 p = patch_row<kBf16>(fa, my_src + 2 * w, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], lo_a, hi_a);
-        lo_a = p.x; hi_a = p.y;
+        for (int i = 0; i < 8; ++i) {
+          bool ti = false;
+          fold(i, fast_pair16<kBf16>(word_of(t.row[i], w), r, mz, lim, ti));
+          tie |= uint32_t(ti) << i;
+        }
+      } else {   // codes of channels far beyond 16 bits: the fp32 clamp
+        const float2 top = make_float2(kMagic + s_maxq[c], kMagic + s_maxq[c + 1]);
+        uint32_t m = 0u;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          uint32_t ca, cb;
+          fast_pair<kBf16>(word_of(t.row[i], w), r, mz, top, m, 1u << i, 1u << (8 + i), ca, cb);
+          fold(i, prmt(ca, cb, 0x5410u));
+        }
+        tie = (m | (m >> 8)) & 0xffu;
       }
-      if (fb) {
-        const uint2 p = patch_row<kBf16>(fb, my_src + 2 * w + 1, a.key_s_tok, s_scale[c + 1], s_zp[c + 1], s_maxq[c + 1], lo_b,
-                                  hi_b);
+      uint32_t lo_a = prmt(l03, l47, 0x0040u) & 0xffffu, lo_b = prmt(l03, l47, 0x0062u) & 0xffffu;
+      uint32_t hi_a = prmt(h03, h47, 0x0040u) & 0xffffu, hi_b = prmt(h03, h47, 0x0062u) & 0xffffu;
+      if (tie) {
+        uint2 p = patch_row<kBf16>(tie, my_src + 2 * w, a.key_s_tok, s_scale[c], s_zp[c], s_maxq[c], lo_a, hi_a);
+        lo_a = p.x; hi_a = p.y;
+        p = patch_row<kBf16>(tie, my_src + 2 * w + 1, a.key_s_tok, s_scale[c + 1], s_zp[c + 1], s_maxq[c + 1], lo_b,
+                             hi_b);
         lo_b = p.x; hi_b = p.y;
       }
       store(c, lo_a, hi_a);
@@ -513,98 +553,197 @@ quantize_key_d128_kernel(const KittyKeyQuantArgs a) {
     reinterpret_cast<uint4*>(out_high)[i] = reinterpret_cast<const uint4*>(s_high)[i];
 }
 
+// The 8 packed bytes of 32 channels of one token (byte j = channels 4 j .. 4 j + 3 at
+// bits 0,2,4,6) from their code words (lane k = code of channel 2 w + k of word w)
+__device__ __forceinline__ uint2 value_bytes(const uint32_t (&wv)[16]) {
+  uint32_t y[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t x = wv[2 * j] + (wv[2 * j + 1] << 4);   // (c0 + 16 c2, c1 + 16 c3) in the lanes
+    y[j] = x + (x >> 14);                                  // byte 0: c0 + 4 c1 + 16 c2 + 64 c3
+  }
+  return make_uint2(prmt(prmt(y[0], y[1], 0x0040u), prmt(y[2], y[3], 0x0040u), 0x5410u),
+                    prmt(prmt(y[4], y[5], 0x0040u), prmt(y[6], y[7], 0x0040u), 0x5410u));
+}
+
+// One token's 32 channels with per-pair near-tie flags and clamped codes: the path for
+// tokens with a near-tie or a code outside 0..3 somewhere (rare), out of line.  Returns
+// the packed bytes and the tie bits (bit c = channel c of the 32).
+template <bool kBf16>
+__device__ __noinline__ uint3 value_token_slow(uint4 a0, uint4 a1, uint4 a2, uint4 a3, float rcp, float zp,
+                                               int wide) {
+  const uint4 v[4] = {a0, a1, a2, a3};
+  const float2 r2 = make_float2(rcp, rcp);
+  const float2 mz = make_float2(kMagic + zp, kMagic + zp);
+  uint32_t wv[16];
+  uint32_t tie = 0u;
+  if (!wide) {
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+      bool ti = false;
+      wv[w] = fast_pair16<kBf16>(word_of(v[w >> 2], w & 3), r2, mz, 0x00030003u, ti);
+      tie |= ti ? (3u << (2 * w)) : 0u;
+    }
+  } else {
+    const float2 top = make_float2(kMagic + 3.0f, kMagic + 3.0f);
+#pragma unroll
+    for (int w = 0; w < 16; ++w) {
+      uint32_t c0, c1;
+      fast_pair<kBf16>(word_of(v[w >> 2], w & 3), r2, mz, top, tie, 1u << (2 * w), 1u << (2 * w + 1), c0, c1);
+      wv[w] = prmt(c0, c1, 0x5410u);
+    }
+  }
+  const uint2 o = value_bytes(wv);
+  return make_uint3(o.x, o.y, tie);
+}
+
+// Value pages, D = G = 128: 256 threads per page-head; thread (tp = tid >> 2, cq = tid & 3)
+// holds tokens 2 tp and 2 tp + 1, channels 32 cq .. 32 cq + 31 (four 16-byte loads per
+// token).  The four lanes of a token reduce its min / max with two shuffles and each
+// computes the token's statistics (same values in all four), so no statistic is
+// broadcast and no shared memory or barrier is needed; each thread packs its 32
+// channels of a token into 8 bytes (byte j = channels 4 j .. 4 j + 3 at bits 0,2,4,6)
+// and stores them directly (the four lanes of a token write its 32-byte row).
 template <bool kBf16, bool kMetaBf16>
-__global__ void __launch_bounds__(kFastThreads, 4)
+__global__ void __launch_bounds__(kFastThreads, KITTY_Q_MINB)
 quantize_value_d128_kernel(const KittyValueQuantArgs a) {
   using T = Half16<kBf16>;
-  constexpr int D4 = 32;
-  __shared__ __align__(16) uint8_t s_codes[128 * D4];
   const int job = blockIdx.x / a.num_heads;
   const int h = blockIdx.x - job * a.num_heads;
-  const int tid = threadIdx.x, tg = tid >> 4, cg = tid & 15;
+  const int tid = threadIdx.x, cq = tid & 3, tp = tid >> 2;
   const uint16_t* src = reinterpret_cast<const uint16_t*>(a.value) + a.value_off[job] + h * a.val_s_head;
   const int n_valid = a.n_valid ? a.n_valid[job] : 128;
   const int64_t page = a.dst_page[job];
   if (page < 0) return;   // skipped job (a batched append flushes only full buffers)
-  Tile8x8 t;
-  load_tile(t, src, a.val_s_tok, tg, cg, n_valid);
   uint16_t* out_scale = reinterpret_cast<uint16_t*>(a.val_scale) + page * a.meta_s_page + h * a.meta_s_head;
   uint16_t* out_zero = reinterpret_cast<uint16_t*>(a.val_zero) + page * a.meta_s_page + h * a.meta_s_head;
-  // per-token min / max over the 16 lanes of the token row; lane cg (< 8) keeps those
-  // of token 8 tg + cg, computes its statistics once, and every lane reads the
-  // statistics of its 8 tokens with shuffles
-  const int mine = cg & 7;
-  float mn_m = 0.0f, mx_m = 0.0f;
-  bool finite = true;
+  uint8_t* out_codes = a.val_codes + page * a.codes_s_page + h * a.codes_s_head;
+  const bool vec = ((reinterpret_cast<uintptr_t>(src) & 15) == 0);
+
+  uint4 v[2][4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    uint32_t lo = T::min2(T::min2(t.row[i].x, t.row[i].y), T::min2(t.row[i].z, t.row[i].w));
-    uint32_t hi = T::max2(T::max2(t.row[i].x, t.row[i].y), T::max2(t.row[i].z, t.row[i].w));
+  for (int k = 0; k < 2; ++k) {
+    const int tok = 2 * tp + k;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v[k][j] = make_uint4(0u, 0u, 0u, 0u);
+    if (tok < n_valid) {
+      const uint16_t* p = src + tok * a.val_s_tok + 32 * cq;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        if (vec) {
+          v[k][j] = reinterpret_cast<const uint4*>(p)[j];
+        } else {
+          const uint16_t* q = p + 8 * j;
+          v[k][j] = make_uint4(uint32_t(q[0]) | (uint32_t(q[1]) << 16), uint32_t(q[2]) | (uint32_t(q[3]) << 16),
+                               uint32_t(q[4]) | (uint32_t(q[5]) << 16), uint32_t(q[6]) | (uint32_t(q[7]) << 16));
+        }
+      }
+    }
+  }
+  // per-token statistics in the reference's float32 sequence (quantize_value.py:62-81):
+  // min / max of both tokens over the four lanes, then lanes with cq even compute token
+  // 2 tp and lanes with cq odd token 2 tp + 1 (the divisions once per token and lane
+  // pair); the partner lane's values come by one shuffle each
+  float mnk[2], mxk[2];
+#pragma unroll
+  for (int k = 0; k < 2; ++k) {
+    uint32_t lo = T::min2(T::min2(v[k][0].x, v[k][0].y), T::min2(v[k][0].z, v[k][0].w));
+    uint32_t hi = T::max2(T::max2(v[k][0].x, v[k][0].y), T::max2(v[k][0].z, v[k][0].w));
+#pragma unroll
+    for (int j = 1; j < 4; ++j) {
+      lo = T::min2(lo, T::min2(T::min2(v[k][j].x, v[k][j].y), T::min2(v[k][j].z, v[k][j].w)));
+      hi = T::max2(hi, T::max2(T::max2(v[k][j].x, v[k][j].y), T::max2(v[k][j].z, v[k][j].w)));
+    }
     lo = T::min2(lo, __funnelshift_l(lo, lo, 16));   // both halves: min of the pair
     hi = T::max2(hi, __funnelshift_l(hi, hi, 16));
     // (min, -max) in one pair: the sign flip of the high half negates it (NaN stays NaN)
     uint32_t mm = (lo & 0x0000ffffu) | ((hi ^ 0x80000000u) & 0xffff0000u);
-#pragma unroll
-    for (int o = 1; o < 16; o <<= 1) mm = T::min2(mm, __shfl_xor_sync(0xffffffffu, mm, o));
+    mm = T::min2(mm, __shfl_xor_sync(0xffffffffu, mm, 1));
+    mm = T::min2(mm, __shfl_xor_sync(0xffffffffu, mm, 2));
     const float2 mmf = T::to_f2(mm);
-    const float mn = mmf.x, mx = -mmf.y;
-    finite = finite && isfinite(mn) && isfinite(mx);
-    mn_m = (mine == i) ? mn : mn_m;
-    mx_m = (mine == i) ? mx : mx_m;
+    mnk[k] = mmf.x;
+    mxk[k] = -mmf.y;
   }
-  const float scale_m = __fdiv_rn(clamp_min(mx_m - mn_m, 1e-8f), 3.0f);
-  const float zp_m = tmin(tmax(rintf(__fdiv_rn(-mn_m, scale_m)), 0.0f), 3.0f);
+  const int mine = cq & 1;
+  const float mn = mine ? mnk[1] : mnk[0], mx = mine ? mxk[1] : mxk[0];
+  const float scale_m = __fdiv_rn(clamp_min(mx - mn, 1e-8f), 3.0f);
+  const float zp_m = tmin(tmax(rintf(__fdiv_rn(-mn, scale_m)), 0.0f), 3.0f);
   const float rcp_m = __frcp_rn(scale_m);
-  if (cg < 8) {
-    out_scale[(8 * tg + cg) * a.meta_s_tok] = Half16<kMetaBf16>::meta(scale_m);
-    out_zero[(8 * tg + cg) * a.meta_s_tok] = Half16<kMetaBf16>::meta(zp_m);
+  // |x| / scale can reach 16000: that token's codes take the fp32 clamp
+  const int wide_m = !(fmaxf(fabsf(mn), fabsf(mx)) * rcp_m < 16000.0f);
+  if (cq < 2) {
+    out_scale[(2 * tp + mine) * a.meta_s_tok] = Half16<kMetaBf16>::meta(scale_m);
+    out_zero[(2 * tp + mine) * a.meta_s_tok] = Half16<kMetaBf16>::meta(zp_m);
   }
-  finite = __all_sync(0xffffffffu, finite);   // warp-uniform: the shuffles below run in every lane
-  const int base_lane = threadIdx.x & 16;
-  uint32_t bits[8];
-  const uint16_t* my_src = src + (8 * tg) * a.val_s_tok + 8 * cg;
-  if (finite) {
-    uint32_t mlo = 0u, mhi = 0u;   // near-tie flags: token i, channel k -> bit 8 (i & 3) + k of mlo (i < 4) / mhi
+  const float scale_o = __shfl_xor_sync(0xffffffffu, scale_m, 1), zp_o = __shfl_xor_sync(0xffffffffu, zp_m, 1);
+  const float rcp_o = __shfl_xor_sync(0xffffffffu, rcp_m, 1);
+  const int wide_o = __shfl_xor_sync(0xffffffffu, wide_m, 1);
+  const float scale[2] = {mine ? scale_o : scale_m, mine ? scale_m : scale_o};
+  const float zp[2] = {mine ? zp_o : zp_m, mine ? zp_m : zp_o};
+  const float rcp[2] = {mine ? rcp_o : rcp_m, mine ? rcp_m : rcp_o};
+  const int wide[2] = {mine ? wide_o : wide_m, mine ? wide_m : wide_o};
+  bool finite = isfinite(mnk[0]) && isfinite(mxk[0]) && isfinite(mnk[1]) && isfinite(mxk[1]);
+  finite = __all_sync(0xffffffffu, finite);   // warp-uniform: the warp takes one path
 #pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float rcp = __shfl_sync(0xffffffffu, rcp_m, base_lane + i);
-      const float zp = __shfl_sync(0xffffffffu, zp_m, base_lane + i);
-      const float2 r2 = make_float2(rcp, rcp);
-      const float2 mz = make_float2(kMagic + zp, kMagic + zp);
-      const float2 top = make_float2(kMagic + 3.0f, kMagic + 3.0f);
-      uint32_t& m = (i < 4) ? mlo : mhi;
-      const int ib = 8 * (i & 3);
-      uint32_t c[8];
+  for (int k = 0; k < 2; ++k) {
+    const int tok = 2 * tp + k;
+    const uint16_t* my_src = src + tok * a.val_s_tok + 32 * cq;
+    uint32_t out0, out1;
+    if (finite) {
+      const float2 r2 = make_float2(rcp[k], rcp[k]);
+      const float2 mz = make_float2(kMagic + zp[k], kMagic + zp[k]);
+      // fast: rint(x r) + zp in 16-bit lanes, one running maximum of the rounding distance
+      // and one OR of the code bits outside 0..3 for the whole token
+      uint32_t tie = 0u;
+      bool slow = wide[k] != 0;
+      if (!slow) {
+        float emax = 0.f;
+        uint32_t bad = 0u;
+        uint32_t wv[16];
 #pragma unroll
-      for (int w = 0; w < 4; ++w)
-        fast_pair<kBf16>(word_of(t.row[i], w), r2, mz, top, m, 1u << (ib + 2 * w), 1u << (ib + 2 * w + 1), c[2 * w],
-                  c[2 * w + 1]);
-      bits[i] = pack4(c[0], c[1], c[2], c[3], 0) | (pack4(c[4], c[5], c[6], c[7], 0) << 8);
-      const uint32_t f = (m >> ib) & 0xffu;
-      const float scale = __shfl_sync(0xffffffffu, scale_m, base_lane + i);
-      if (f && 8 * tg + i < n_valid)
-        bits[i] = patch_row<kBf16>(f, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, bits[i], 0u).x;
-    }
-  } else {   // non-finite statistics in this warp: the exact path (rows beyond n_valid read as zeros)
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      const float scale = __shfl_sync(0xffffffffu, scale_m, base_lane + i);
-      const float zp = __shfl_sync(0xffffffffu, zp_m, base_lane + i);
-      uint32_t b;
-      if (8 * tg + i < n_valid) {
-        b = patch_row<kBf16>(0xffu, my_src + i * a.val_s_tok, 1, scale, zp, 3.0f, 0u, 0u).x;
-      } else {
-        b = (quant_code(0.0f, scale, zp, 3.0f) & 3u) * 0x5555u;
+        for (int w = 0; w < 16; ++w) {
+          const float2 x = T::to_f2(word_of(v[k][w >> 2], w & 3));
+          const float2 f = fma2(x, r2, mz);
+          const float2 e = fma2(x, r2, fma2(f, make_float2(-1.0f, -1.0f), mz));
+          asm("max.f32 %0, %1, %2, %3;" : "=f"(emax) : "f"(emax), "f"(fabsf(e.x)), "f"(fabsf(e.y)));
+          wv[w] = prmt(__float_as_uint(f.x), __float_as_uint(f.y), 0x5410u);
+          bad |= wv[w];
+        }
+        const uint2 o = value_bytes(wv);
+        out0 = o.x;
+        out1 = o.y;
+        slow = emax > kNearHalf || (bad & 0xfffcfffcu) != 0u;
       }
-      bits[i] = b;
-    }
-  }
+      if (slow) {   // a near-tie or a code outside 0..3 in this token: per-pair flags and clamps
+        const uint3 r = value_token_slow<kBf16>(v[k][0], v[k][1], v[k][2], v[k][3], rcp[k], zp[k], wide[k]);
+        out0 = r.x;
+        out1 = r.y;
+        tie = r.z;
+      }
+      if (tie && tok < n_valid) {   // near-ties: exact codes of the flagged channels (8 per call)
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
-    *reinterpret_cast<uint16_t*>(s_codes + (8 * tg + i) * D4 + 2 * cg) = uint16_t(bits[i]);
-  __syncthreads();
-  uint8_t* out = a.val_codes + page * a.codes_s_page + h * a.codes_s_head;
-  reinterpret_cast<uint4*>(out)[tid] = reinterpret_cast<const uint4*>(s_codes)[tid];
+        for (int g = 0; g < 4; ++g) {
+          const uint32_t f = (tie >> (8 * g)) & 0xffu;
+          if (f) {
+            uint32_t& o = g < 2 ? out0 : out1;
+            const int sh = 16 * (g & 1);
+            const uint32_t b = patch_row<kBf16>(f, my_src + 8 * g, 1, scale[k], zp[k], 3.0f, (o >> sh) & 0xffffu, 0u).x;
+            o = (o & ~(0xffffu << sh)) | ((b & 0xffffu) << sh);
+          }
+        }
+      }
+    } else {   // non-finite statistics in this warp: the exact path (tokens beyond n_valid read as zeros)
+      uint32_t g16[4];
+#pragma unroll
+      for (int g = 0; g < 4; ++g) {
+        g16[g] = tok < n_valid ? patch_row<kBf16>(0xffu, my_src + 8 * g, 1, scale[k], zp[k], 3.0f, 0u, 0u).x
+                               : (quant_code(0.0f, scale[k], zp[k], 3.0f) & 3u) * 0x5555u;
+      }
+      out0 = (g16[0] & 0xffffu) | (g16[1] << 16);
+      out1 = (g16[2] & 0xffffu) | (g16[3] << 16);
+    }
+    *reinterpret_cast<uint2*>(out_codes + tok * 32 + 8 * cq) = make_uint2(out0, out1);
+  }
 }
 
 bool fast_source_ok(const void* base, const int64_t s_tok, const int64_t s_ch) {
