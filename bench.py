@@ -897,7 +897,7 @@ def quantize_arm(args, spec, d, device, local):
 def decode_kernel_name(variant, g, D, G, fp16_regions=True):
     """Kernel family a decode call runs (the library's choice for "auto"; the tcgen05
     family takes pages-only calls and falls back to the library's choice otherwise)."""
-    i8 = D == 128 and G == 128 and g <= 8
+    i8 = D == 128 and G == 128 and g <= 16   # above 8 query heads per KV head: in passes of 8
     if variant == "tc" and i8 and not fp16_regions:
         return "decode_tc_kernel"
     if variant in ("auto", "tc", "int8"):

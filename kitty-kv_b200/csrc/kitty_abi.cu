@@ -71,6 +71,8 @@ int choose_variant(const KittyDecodeArgs* a) {
 void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
   plan->variant = choose_variant(a);
   plan->grid = 0;
+  plan->qh_base = 0;
+  plan->g_pass = 0;
   plan->ws_m = plan->ws_l = plan->ws_o = nullptr;
   plan->ws_count = nullptr;
   if (plan->variant == 3) {
@@ -78,6 +80,9 @@ void make_plan(const KittyDecodeArgs* a, DecodePlan* plan) {
     return;
   }
   if (plan->variant == 2) {
+    // more than kI8MaxHeadsPerPass query heads per KV head run in passes of that many
+    const int g = a->num_q_heads / a->num_kv_heads;
+    if (g > kI8MaxHeadsPerPass) plan->g_pass = kI8MaxHeadsPerPass;
     i8_plan(*a, device_sm_count(), plan);
     return;
   }
@@ -214,6 +219,21 @@ int kitty_paged_decode(const KittyDecodeArgs* args, void* stream) {
     if (plan.variant >= 1) plan.ws_count = reinterpret_cast<int*>(w + 2 * up(n * 4) + up(n * args->head_dim * 4));
   }
   cudaStream_t s = as_stream(stream);
+  if (plan.variant == 2 && plan.g_pass > 0) {
+    // the integer kernel in passes over the query heads of each KV head (the workspace,
+    // sized for all heads, is reused pass after pass on the same stream)
+    const int g = args->num_q_heads / args->num_kv_heads;
+    for (int qb = 0; qb < g; qb += kI8MaxHeadsPerPass) {
+      DecodePlan pp = plan;
+      pp.qh_base = qb;
+      pp.g_pass = std::min(kI8MaxHeadsPerPass, g - qb);
+      rc = launch_decode_i8(*args, pp, s);
+      if (rc != KITTY_OK) return rc;
+      rc = launch_decode_merge(*args, pp, s);
+      if (rc != KITTY_OK) return rc;
+    }
+    return KITTY_OK;
+  }
   rc = plan.variant == 3   ? launch_decode_tc(*args, plan, s)
        : plan.variant == 2 ? launch_decode_i8(*args, plan, s)
                            : launch_decode_simt(*args, plan, s);

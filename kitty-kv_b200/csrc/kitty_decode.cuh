@@ -22,6 +22,8 @@ struct DecodePlan {
   int variant;        // 0 = CUDA-core (any shape), 2 = integer mma.sync (D = G = 128, g <= 8),
                       // 3 = integer tcgen05 / tensor memory (D = G = 128, g <= 8, pages only)
   int grid;           // tensor-core variant: CTAs of the persistent grid
+  int qh_base;        // integer mma.sync variant in passes: first query head (of each KV head's
+  int g_pass;         //   group) this launch covers, and how many (0: all g = Hq / H)
   float* ws_m;        // [B][H][S][g] running max per split (natural log units)
   float* ws_l;        // [B][H][S][g] running sum per split
   float* ws_o;        // [B][H][S][g][D] unnormalised accumulator per split
@@ -38,6 +40,8 @@ int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStrea
 bool i8_supports(const KittyDecodeArgs& a);
 int i8_ctas_per_sm();
 void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan);
+// query heads per KV head one integer-kernel launch handles (more run in passes)
+constexpr int kI8MaxHeadsPerPass = 8;
 int read_decode_error_i8(uint32_t* flags, int clear);
 int launch_decode_tc(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream);
 bool tc_supports(const KittyDecodeArgs& a);

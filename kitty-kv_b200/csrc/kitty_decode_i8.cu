@@ -301,15 +301,15 @@ __device__ __forceinline__ void softmax_step(State& st, float (&s)[16]) {
 // shared memory rather than registers (read once per page by the digit step), and the
 // boosted-entry table.  Returns the number of boosted entries.
 template <int kQG>
-__device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, uint8_t* wsm, const Layout& L,
-                             int lane) {
+__device__ int setup_segment(const KittyDecodeArgs& a, int b, int h, int g, int g_all, int qb, uint8_t* wsm,
+                             const Layout& L, int lane) {
   const int pq = lane >> 3, cb = lane & 7;
 #pragma unroll
   for (int qg = 0; qg < kQG; ++qg) {
     uint4 x0 = make_uint4(0u, 0u, 0u, 0u), x1 = x0;
     if (pq + 4 * qg < g) {
       const uint4* src = reinterpret_cast<const uint4*>(reinterpret_cast<const uint16_t*>(a.q) + b * a.q_s_seq +
-                                                        int64_t(h * g + pq + 4 * qg) * a.q_s_head + 16 * cb);
+                                                        int64_t(h * g_all + qb + pq + 4 * qg) * a.q_s_head + 16 * cb);
       x0 = src[0];
       x1 = src[1];
     }
@@ -495,7 +495,9 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   using T = Half16<kBf16>;
   extern __shared__ __align__(128) uint8_t smem[];
   const int K = a.d_boost, H = a.num_kv_heads, B = a.batch;
-  const int g = a.num_q_heads / H;
+  // this launch's query heads: qb .. qb + g - 1 of every KV head's group of g_all
+  const int g_all = a.num_q_heads / H;
+  const int g = plan.g_pass > 0 ? plan.g_pass : g_all, qb = plan.qh_base;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int g_ = lane >> 2, q_ = lane & 3;
   const int pq = lane >> 3, cb = lane & 7;
@@ -607,7 +609,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   State st[kQG];
 #pragma unroll
   for (int qg = 0; qg < kQG; ++qg) reset_state(st[qg]);
-  int nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane);
+  int nb = setup_segment<kQG>(a, pos.b, pos.h, g, g_all, qb, wsm, L, lane);
 
   // ldmatrix row addresses: row `lane` of a 32-row k-step of the key / value plane
   const uint32_t k_row = smem_u32(kbuf) + 32u * lane, v_row = smem_u32(vbuf) + 32u * lane;
@@ -994,7 +996,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
     if (seg_end) {
       slot = 0;
       __syncwarp();
-      nb = setup_segment<kQG>(a, pos.b, pos.h, g, wsm, L, lane);
+      nb = setup_segment<kQG>(a, pos.b, pos.h, g, g_all, qb, wsm, L, lane);
     }
   }
   if (failed) {
@@ -1012,7 +1014,7 @@ bool i8_supports(const KittyDecodeArgs& a) {
   auto region_ok = [](const void* p, int64_t s_seq, int64_t s_head, int64_t s_tok) {
     return p == nullptr || (aligned(p, 16) && s_seq % 8 == 0 && s_head % 8 == 0 && s_tok % 8 == 0);
   };
-  return a.head_dim == kD && a.group == kG && g >= 1 && g <= 8 && a.d_boost <= 128 &&
+  return a.head_dim == kD && a.group == kG && g >= 1 && g <= 2 * kI8MaxHeadsPerPass && a.d_boost <= 128 &&
          aligned(a.q, 16) && a.q_s_seq % 8 == 0 && a.q_s_head % 8 == 0 &&
          region_ok(a.sink_k, a.sk_s_seq, a.sk_s_head, a.sk_s_tok) &&
          region_ok(a.sink_v, a.sv_s_seq, a.sv_s_head, a.sv_s_tok) &&
@@ -1026,7 +1028,11 @@ bool i8_supports(const KittyDecodeArgs& a) {
 int i8_ctas_per_sm() { return 1; }
 
 namespace {
-int i8_groups(const KittyDecodeArgs& a) { return a.num_q_heads / a.num_kv_heads > 4 ? 2 : 1; }
+// groups of four query heads per launch (a launch covers at most kI8MaxHeadsPerPass)
+int i8_pass_heads(const KittyDecodeArgs& a, const DecodePlan& plan) {
+  return plan.g_pass > 0 ? plan.g_pass : std::min(a.num_q_heads / a.num_kv_heads, kI8MaxHeadsPerPass);
+}
+int i8_groups(const KittyDecodeArgs& a, const DecodePlan& plan) { return i8_pass_heads(a, plan) > 4 ? 2 : 1; }
 int i8_warps(int qg) { return qg == 1 ? warps_per_cta<1>() : warps_per_cta<2>(); }
 int i8_ctas(int qg) { return qg == 1 ? ctas_per_sm<1>() : ctas_per_sm<2>(); }
 }  // namespace
@@ -1040,7 +1046,7 @@ void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   const int items_max = a.max_pages_per_seq + kFp16Weight * dev::kMaxFp16Items;
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
-  const int qg = i8_groups(a);
+  const int qg = i8_groups(a, *plan);
   const int64_t warps = int64_t(sm_count) * i8_ctas(qg) * i8_warps(qg);
   const int64_t per_warp = std::max<int64_t>(1, int64_t(a.batch) * a.num_kv_heads * items_max / warps);
   const int auto_target = int(std::max<int64_t>(kSlotsTarget, (items_max + per_warp - 1) / per_warp));
@@ -1087,7 +1093,7 @@ int prepare_i8(int smem, int* blocks) {
 }  // namespace
 
 int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
-  const int qg = i8_groups(a);
+  const int qg = i8_groups(a, plan);
   const Layout L = i8_layout(a.d_boost, qg);
   const int warps = i8_warps(qg);
   const int smem = warps * L.size;

@@ -275,9 +275,13 @@ decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   __shared__ float s_w[kMergeMaxSlots];
   __shared__ float s_red[kMergeThreads / 32];
   __shared__ float s_M, s_L;
-  const int b = blockIdx.y, qhg = blockIdx.x;  // global query head
-  const int H = a.num_kv_heads, g = a.num_q_heads / H, D = a.head_dim;
-  const int h = qhg / g, qh = qhg - h * g;
+  // blockIdx.x = query head within the launch's heads: g of every KV head's group of g_all,
+  // starting at plan.qh_base (all of them unless the integer kernel ran in passes)
+  const int b = blockIdx.y;
+  const int H = a.num_kv_heads, g_all = a.num_q_heads / H, D = a.head_dim;
+  const int g = plan.g_pass > 0 ? plan.g_pass : g_all;
+  const int h = blockIdx.x / g, qh = blockIdx.x - h * g;
+  const int qhg = h * g_all + plan.qh_base + qh;   // global query head
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int64_t base = (int64_t(b) * H + h) * plan.num_splits;
   // slots written for this (sequence, head): all of them, or the recorded count
@@ -380,7 +384,8 @@ int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStr
 }
 
 int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
-  dim3 grid(a.num_q_heads, a.batch);
+  const int g = plan.g_pass > 0 ? plan.g_pass : a.num_q_heads / a.num_kv_heads;
+  dim3 grid(a.num_kv_heads * g, a.batch);
   if (plan.num_splits > kMergeMaxSlots)
     return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: more than 1024 partial slots per sequence and head");
   decode_merge_kernel<<<grid, kMergeThreads, 0, stream>>>(a, plan);

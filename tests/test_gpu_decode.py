@@ -234,3 +234,29 @@ def test_tcgen05_family_on_pages_only_batches(hq, rate):
         exp = O.paged_attention(case.q[b], pages, *np_pools, case.boost_idx, case.d_boost, z, z, z, z, hq, H_, D)
         assert_close(outs["tc"][b], exp)
     assert_close(outs["tc"], outs["int8"])
+
+
+@pytest.mark.parametrize("hq,rate,splits", [(96, 0.125, 0), (128, 0.25, 0), (128, 0.125, 3), (80, 0.125, 1)])
+def test_integer_family_beyond_eight_query_heads(hq, rate, splits):
+    """More than 8 query heads per KV head (GQA 10:1, 12:1, 16:1): the integer kernel runs
+    in passes of up to 8 query heads per KV head (each pass its own launch and merge), and
+    must agree with the oracle on a mixed batch with sinks, ragged tails and permuted
+    pages at several split counts."""
+    H = 8
+    ctx = [32 + 7 * 128 + 50, 32 + 2 * 128 + 127, 32 + 11 * 128, 40]
+    case = synthetic.make_decode_case(400 + hq, len(ctx), hq, H, 128, ctx, boost_rate=rate)
+    total = sum(s.n_pages for s in case.seqs)
+    n_phys = total + 4
+    phys_of = GC.phys_layout(case, 401, n_phys)
+    pools = build_pools_gpu(case, phys_of, n_phys)
+    sk, sv, sl, tk, tv, tl = GC.padded_regions(case)
+    bt, npg = GC.block_table(case, phys_of)
+    prev = KK._lib.force_decode_variant("int8")
+    try:
+        got = run_batched(case, pools, phys_of, num_splits=splits)
+    finally:
+        KK._lib.force_decode_variant(prev)
+    assert KK._lib.device_error_flags() == 0
+    exp = O.paged_attention_batched(case.q, bt, npg, tuple(p.cpu().numpy() for p in pools), case.boost_idx,
+                                    case.d_boost, sk, sv, sl, tk, tv, tl)
+    assert_close(got, exp)
