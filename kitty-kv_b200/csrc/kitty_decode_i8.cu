@@ -61,21 +61,27 @@ namespace {
 
 using namespace dev;
 
-// Resident warps per SM: 12 with up to 4 query heads per KV head (<= 170 registers),
-// as one CTA: warps of one CTA share a scheduling age, while with three CTAs of four
-// the oldest CTA's warps won the issue slots and finished well before the youngest,
-// which then set the kernel's end (config 2: 1.5 % slower).  With 8 query heads (255
-// registers) 8 warps per SM, as two CTAs of four (7 % faster than one CTA of eight).
+// Resident warps per SM: 12 (<= 170 registers), as one CTA: warps of one CTA share a
+// scheduling age, while with three CTAs of four the oldest CTA's warps won the issue
+// slots and finished well before the youngest, which then set the kernel's end (4 query
+// heads per KV head, config 2: 1.5 % slower; 8 heads, config 4: 1.5 % slower, and two
+// CTAs of six 3 % slower).  With 8 query heads the 168-register cap costs a few spills
+// but 12 warps still beat 8 warps at 245 registers by 5 %.  A CTA whose warps' shared
+// memory exceeds the per-CTA limit (8 heads with many boosted channels) is launched
+// with fewer warps (the kernel reads its warp count from blockDim).
 #ifndef KITTY_I8_W1
 #define KITTY_I8_W1 12
 #endif
-#ifndef KITTY_I8_SPLIT1
-#define KITTY_I8_SPLIT1 0
+#ifndef KITTY_I8_W2
+#define KITTY_I8_W2 12
+#endif
+#ifndef KITTY_I8_C2
+#define KITTY_I8_C2 1
 #endif
 template <int kQG>
-__host__ __device__ constexpr int warps_per_cta() { return kQG == 1 ? KITTY_I8_W1 : 4; }
+__host__ __device__ constexpr int warps_per_cta() { return kQG == 1 ? KITTY_I8_W1 : KITTY_I8_W2; }
 template <int kQG>
-__host__ __device__ constexpr int ctas_per_sm() { return kQG == 1 ? 1 : 2; }
+__host__ __device__ constexpr int ctas_per_sm() { return kQG == 1 ? 1 : KITTY_I8_C2; }
 constexpr int kD = 128, kG = 128;
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
@@ -141,6 +147,27 @@ __device__ __forceinline__ void mma_k16(int (&c)[4], uint32_t a0, uint32_t a1, u
       : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
       : "r"(a0), "r"(a1), "r"(b0));
 }
+// A unsigned, B signed (the signed top key digit)
+template <bool kFirst>
+__device__ __forceinline__ void mma_k32s(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                         uint32_t b0, uint32_t b1) {
+  if (kFirst)
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%10,%10,%10,%10};\n"
+        : "=r"(c[0]), "=r"(c[1]), "=r"(c[2]), "=r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "r"(0));
+  else
+    asm volatile(
+        "mma.sync.aligned.m16n8k32.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, {%0,%1,%2,%3};\n"
+        : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+        : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+__device__ __forceinline__ void mma_k16s(int (&c)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.s32.u8.s8.s32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};\n"
+      : "+r"(c[0]), "+r"(c[1]), "+r"(c[2]), "+r"(c[3])
+      : "r"(a0), "r"(a1), "r"(b0));
+}
 __device__ __forceinline__ void mma_f16(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                         uint32_t b0, uint32_t b1) {
   asm volatile(
@@ -184,6 +211,10 @@ template <int i>
 __device__ __forceinline__ uint32_t high_code(uint32_t t) {   // 4 * key_code factor
   return i < 3 ? ((t << 2) & (0x0C0C0C0Cu << (2 * i))) : (t & 0xC0C0C0C0u);
 }
+// the same with the code index as an argument (a constant after unrolling)
+__device__ __forceinline__ uint32_t high_code_of(int i, uint32_t t) {
+  return i < 3 ? ((t << 2) & (0x0C0C0C0Cu << (2 * i))) : (t & 0xC0C0C0C0u);
+}
 // bytes k of v0..v3 packed into one word
 __device__ __forceinline__ void bytes01(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3, uint32_t& w0,
                                         uint32_t& w1) {
@@ -193,6 +224,13 @@ __device__ __forceinline__ void bytes01(uint32_t v0, uint32_t v1, uint32_t v2, u
 }
 __device__ __forceinline__ uint32_t byte2(uint32_t v0, uint32_t v1, uint32_t v2, uint32_t v3) {
   return prmt(prmt(v0, v1, 0x0062u), prmt(v2, v3, 0x0062u), 0x5410u);
+}
+
+// Top key digits b2 in [0, 128) (offset binary: the digit value is b2 - 64) as signed
+// bytes b2 - 64: flip bit 6 and copy the flipped bit 6 into bit 7, byte by byte.
+__device__ __forceinline__ uint32_t signed_top_digits(uint32_t b2) {
+  const uint32_t t = b2 ^ 0x40404040u;
+  return t | ((t & 0x40404040u) << 1);
 }
 
 // One 32-channel k-step of the key baseline plane (K index = channel 32 ks + k) into
@@ -487,8 +525,8 @@ __device__ void process_fp16_region(const KittyDecodeArgs& a, int b, int h, int 
 
 // kQG groups of four query heads per KV head share each page-head's unpacked
 // operands: with kQG = 2 the key contraction runs one 64-token half at a time
-// (four accumulator sets: two groups x (byte 1, byte 0 | byte 2, code sum)) and the
-// value contraction one 64-channel half at a time.
+// (three accumulator sets: the two groups' bytes 1 | 0 and both groups' signed byte 2)
+// and the value contraction one 64-channel half at a time.
 template <bool kBf16, int kQG>
 __global__ void __launch_bounds__(32 * warps_per_cta<kQG>(), ctas_per_sm<kQG>())
 decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
@@ -514,7 +552,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   // ---- this warp's slice of the item space
   // slice index: warp-major over the CTAs, so a small job spreads over many SMs
   const int64_t gw = int64_t(warp) * gridDim.x + blockIdx.x;
-  const int64_t n_warps = int64_t(gridDim.x) * warps_per_cta<kQG>();
+  const int64_t n_warps = int64_t(gridDim.x) * (blockDim.x >> 5);
   // (units: pages count 1, fp16 chunk items kFp16Weight)
   SegmentScan sc = scan_segments(a, B, H, 0, lane, kFp16Weight);
   const int64_t total = sc.total;
@@ -681,6 +719,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         for (int qq = 0; qq < 4; ++qq) {
           bytes01(fb[4 * qq], fb[4 * qq + 1], fb[4 * qq + 2], fb[4 * qq + 3], d0[qq], d1[qq]);
           d2[qq] = byte2(fb[4 * qq], fb[4 * qq + 1], fb[4 * qq + 2], fb[4 * qq + 3]);
+          if constexpr (kQG == 2) d2[qq] = signed_top_digits(d2[qq]);
         }
         uint8_t* row = dtab + (pq + 4 * qg) * kRow + 16 * cb;
         *reinterpret_cast<uint4*>(row) = make_uint4(d0[0], d0[1], d0[2], d0[3]);
@@ -698,7 +737,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       // ---- scores (log2 domain): s[qg][4 k + i] <-> token 32 k + 4 g_ + i; tile 4 half + i
       // holds tokens 64 half + 4 g_ + i (row g_, k = 2 half) and + 32 (row g_ + 8)
       float s[kQG][16];
-      if constexpr (kQG == 1 && !KITTY_I8_SPLIT1) {
+      if constexpr (kQG == 1) {
       const float zq = zqg[0], cq = cqg[0];
       int acc1[8][4], acc2[8][4];
       // ---- baseline plane
@@ -749,24 +788,23 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         }
       }
       } else {
-        // two query groups, one 64-token half at a time
-        const uint8_t* kb1g[kQG];
-        const uint8_t* kb2g[kQG];
-#pragma unroll
-        for (int qg = 0; qg < kQG; ++qg) { kb1g[qg] = kb1 + 4 * qg * kRow; kb2g[qg] = kb2 + 4 * qg * kRow; }
+        // 8 query heads: this lane's heads q_ (group 0) and q_ + 4 (group 1).  Digits b1 | b0
+        // of a group in one MMA per code plane (column g_: head (g_ >> 1) + 4 qg, digit hi /
+        // lo, as for 4 heads); the signed top digits b2 - 64 of both groups in one more
+        // (column g_: head (g_ >> 1) + 4 (g_ & 1)), so C columns 2 q_ / 2 q_ + 1 of a thread
+        // hold the b2 sums of its heads q_ / q_ + 4 and no all-ones column is needed.
+        // (Splitting the four code planes of a half into two passes, for fewer live
+        // accumulators, re-reads the digits and was 7 % slower.)
+        const uint8_t* kb2s = dtab + 2 * kPlane + ((g_ >> 1) + 4 * (g_ & 1)) * kRow;
 #pragma unroll
         for (int half = 0; half < 2; ++half) {
-          int a1[kQG][4][4], a2[kQG][4][4];
+          int a1[2][4][4], a2[4][4];
 #pragma unroll
           for (int ks = 0; ks < 4; ++ks) {
-            uint32_t b1[kQG][2], b2[kQG][2];
-#pragma unroll
-            for (int qg = 0; qg < kQG; ++qg) {
-              b1[qg][0] = lds32(kb1g[qg] + 32 * ks + 4 * q_);
-              b1[qg][1] = lds32(kb1g[qg] + 32 * ks + 16 + 4 * q_);
-              b2[qg][0] = ones_col ? 0x01010101u : lds32(kb2g[qg] + 32 * ks + 4 * q_);
-              b2[qg][1] = ones_col ? 0x01010101u : lds32(kb2g[qg] + 32 * ks + 16 + 4 * q_);
-            }
+            const uint32_t b10 = lds32(kb1 + 32 * ks + 4 * q_), b11 = lds32(kb1 + 32 * ks + 16 + 4 * q_);
+            const uint32_t b12 = lds32(kb1 + 4 * kRow + 32 * ks + 4 * q_);
+            const uint32_t b13 = lds32(kb1 + 4 * kRow + 32 * ks + 16 + 4 * q_);
+            const uint32_t b20 = lds32(kb2s + 32 * ks + 4 * q_), b21 = lds32(kb2s + 32 * ks + 16 + 4 * q_);
             uint32_t r[4];
             ldsm_t_x2(k_row + 1024u * ks + 16u * half, r);
 #pragma unroll
@@ -775,59 +813,46 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
               const int sh = i < 3 ? 0 : 2;
               const uint32_t c0 = (r[0] >> sh) & m, c1 = (r[1] >> sh) & m, c2 = (r[2] >> sh) & m,
                              c3 = (r[3] >> sh) & m;
-#pragma unroll
-              for (int qg = 0; qg < kQG; ++qg) {
-                if (ks == 0) {
-                  mma_k32_z(a1[qg][i], c0, c1, c2, c3, b1[qg][0], b1[qg][1]);
-                  mma_k32_z(a2[qg][i], c0, c1, c2, c3, b2[qg][0], b2[qg][1]);
-                } else {
-                  mma_k32(a1[qg][i], c0, c1, c2, c3, b1[qg][0], b1[qg][1]);
-                  mma_k32(a2[qg][i], c0, c1, c2, c3, b2[qg][0], b2[qg][1]);
-                }
+              if (ks == 0) {
+                mma_k32_z(a1[0][i], c0, c1, c2, c3, b10, b11);
+                mma_k32_z(a1[1][i], c0, c1, c2, c3, b12, b13);
+                mma_k32s<true>(a2[i], c0, c1, c2, c3, b20, b21);
+              } else {
+                mma_k32(a1[0][i], c0, c1, c2, c3, b10, b11);
+                mma_k32(a1[1][i], c0, c1, c2, c3, b12, b13);
+                mma_k32s<false>(a2[i], c0, c1, c2, c3, b20, b21);
               }
             }
           }
           for (int bs = 0; bs < nb; bs += 16) {
             const uint4 e4 = *reinterpret_cast<const uint4*>(ent + bs + 4 * q_);
             const uint32_t es[4] = {e4.x, e4.y, e4.z, e4.w};
-            uint32_t r[4], bb1[kQG], bb2[kQG];
-#pragma unroll
-            for (int qg = 0; qg < kQG; ++qg) bb1[qg] = bb2[qg] = 0u;
+            uint32_t r[4], bb10 = 0u, bb11 = 0u, bb2 = 0u;
             ldsm_t_x2(smem_u32(kh) + (ent[bs + (lane & 15)] & 0xffffu) + 16u * (lane >> 4), r);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk) {
               const uint32_t pos = es[kk] >> 16;
-#pragma unroll
-              for (int qg = 0; qg < kQG; ++qg) {
-                bb1[qg] |= uint32_t(kb1g[qg][pos]) << (8 * kk);
-                bb2[qg] |= uint32_t(kb2g[qg][pos]) << (8 * kk);
-              }
-            }
-            if (ones_col) {
-#pragma unroll
-              for (int qg = 0; qg < kQG; ++qg) bb2[qg] = 0x01010101u;
+              bb10 |= uint32_t(kb1[pos]) << (8 * kk);
+              bb11 |= uint32_t(kb1[4 * kRow + pos]) << (8 * kk);
+              bb2 |= uint32_t(kb2s[pos]) << (8 * kk);
             }
             const uint32_t x0 = r[2 * half], x1 = r[2 * half + 1];
 #pragma unroll
-            for (int qg = 0; qg < kQG; ++qg) {
-              mma_k16(a1[qg][0], high_code<0>(x0), high_code<0>(x1), bb1[qg]);
-              mma_k16(a2[qg][0], high_code<0>(x0), high_code<0>(x1), bb2[qg]);
-              mma_k16(a1[qg][1], high_code<1>(x0), high_code<1>(x1), bb1[qg]);
-              mma_k16(a2[qg][1], high_code<1>(x0), high_code<1>(x1), bb2[qg]);
-              mma_k16(a1[qg][2], high_code<2>(x0), high_code<2>(x1), bb1[qg]);
-              mma_k16(a2[qg][2], high_code<2>(x0), high_code<2>(x1), bb2[qg]);
-              mma_k16(a1[qg][3], high_code<3>(x0), high_code<3>(x1), bb1[qg]);
-              mma_k16(a2[qg][3], high_code<3>(x0), high_code<3>(x1), bb2[qg]);
+            for (int i = 0; i < 4; ++i) {
+              const uint32_t h0 = high_code_of(i, x0), h1 = high_code_of(i, x1);
+              mma_k16(a1[0][i], h0, h1, bb10);
+              mma_k16(a1[1][i], h0, h1, bb11);
+              mma_k16s(a2[i], h0, h1, bb2);
             }
           }
 #pragma unroll
-          for (int qg = 0; qg < kQG; ++qg)
+          for (int qg = 0; qg < 2; ++qg)
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
               const float f = cqg[qg] * (i == 0 ? 1.0f : i == 1 ? 0.25f : 0.0625f);
               const float2 fl = make_float2(f, f), fh = make_float2(f * 65536.0f, f * 65536.0f);
               const int lo0 = 256 * a1[qg][i][0] + a1[qg][i][1], lo1 = 256 * a1[qg][i][2] + a1[qg][i][3];
-              const int hi0 = a2[qg][i][0] - 64 * a2[qg][i][1], hi1 = a2[qg][i][2] - 64 * a2[qg][i][3];
+              const int hi0 = a2[i][qg], hi1 = a2[i][2 + qg];
               const float2 t = fma2(make_float2(float(lo0), float(lo1)), fl, make_float2(-zqg[qg], -zqg[qg]));
               const float2 rr = fma2(make_float2(float(hi0), float(hi1)), fh, t);
               s[qg][8 * half + i] = rr.x;
@@ -835,22 +860,23 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
             }
         }
       }
-      if constexpr (kQG != 1 || KITTY_I8_SPLIT1) next_keys();
+      if constexpr (kQG != 1) next_keys();
 
       if (!mbar_wait(bar_v, v_phase)) { failed = true; break; }
       v_phase ^= 1u;
       bool v_requested = false;
       if (valid) {
         // ---- P' = p * scale_v as 16-bit fixed point, tokens 32 k + 4 g_ + i (v = 4 k + i)
+        float dvg[kQG];
+#pragma unroll
+        for (int qg = 0; qg < kQG; ++qg) {
+        // (scale, zero) of this lane's tokens, read again for every query group
         uint32_t sz[16];
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           const uint4 x = *reinterpret_cast<const uint4*>(vbuf + 4096 + 4 * (32 * k + 4 * g_));
           sz[4 * k] = x.x; sz[4 * k + 1] = x.y; sz[4 * k + 2] = x.z; sz[4 * k + 3] = x.w;
         }
-        float dvg[kQG];
-#pragma unroll
-        for (int qg = 0; qg < kQG; ++qg) {
         softmax_step(st[qg], s[qg]);   // s -> p
         float pp[16];
 #pragma unroll
@@ -893,7 +919,7 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
         }
         }
         __syncwarp();
-        if constexpr (kQG == 1 && !KITTY_I8_SPLIT1) {
+        if constexpr (kQG == 1) {
         const float dv = dvg[0];
         State& sto = st[0];
         // ---- values: M = channels, K = tokens 32 ks + k
@@ -1033,7 +1059,22 @@ int i8_pass_heads(const KittyDecodeArgs& a, const DecodePlan& plan) {
   return plan.g_pass > 0 ? plan.g_pass : std::min(a.num_q_heads / a.num_kv_heads, kI8MaxHeadsPerPass);
 }
 int i8_groups(const KittyDecodeArgs& a, const DecodePlan& plan) { return i8_pass_heads(a, plan) > 4 ? 2 : 1; }
-int i8_warps(int qg) { return qg == 1 ? warps_per_cta<1>() : warps_per_cta<2>(); }
+// warps of one CTA: the compile-time count, fewer when their shared memory would pass
+// the per-CTA limit of the current device
+int i8_warps(int qg, int d_boost) {
+  static int optin = 0;
+  if (optin == 0) {
+    int dev = 0, v = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&v, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev) != cudaSuccess || v <= 0) {
+      cudaGetLastError();
+      v = 227 * 1024;
+    }
+    optin = v;
+  }
+  const int w = qg == 1 ? warps_per_cta<1>() : warps_per_cta<2>();
+  return std::max(1, std::min(w, optin / i8_layout(d_boost, qg).size));
+}
 int i8_ctas(int qg) { return qg == 1 ? ctas_per_sm<1>() : ctas_per_sm<2>(); }
 }  // namespace
 
@@ -1047,7 +1088,7 @@ void i8_plan(const KittyDecodeArgs& a, int sm_count, DecodePlan* plan) {
   // few segments (small batch, few KV heads per GPU): more slots per segment so that
   // every warp of the persistent grid gets a slice
   const int qg = i8_groups(a, *plan);
-  const int64_t warps = int64_t(sm_count) * i8_ctas(qg) * i8_warps(qg);
+  const int64_t warps = int64_t(sm_count) * i8_ctas(qg) * i8_warps(qg, a.d_boost);
   const int64_t per_warp = std::max<int64_t>(1, int64_t(a.batch) * a.num_kv_heads * items_max / warps);
   const int auto_target = int(std::max<int64_t>(kSlotsTarget, (items_max + per_warp - 1) / per_warp));
   int target = a.num_splits > 0 ? a.num_splits : auto_target;
@@ -1066,7 +1107,7 @@ namespace {
 // shared-memory attribute and resident CTAs per SM of one instantiation, set up once
 // per shared-memory size
 template <bool kBf16, int kQG>
-int prepare_i8(int smem, int* blocks) {
+int prepare_i8(int threads, int smem, int* blocks) {
   static int configured_bytes = 0;
   if (configured_bytes < smem) {
     cudaError_t e =
@@ -1078,8 +1119,7 @@ int prepare_i8(int smem, int* blocks) {
   static int occ_smem = -1, occ_blocks = 1;
   if (occ_smem != smem) {
     int n = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16, kQG>, 32 * warps_per_cta<kQG>(),
-                                                      smem) != cudaSuccess ||
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, decode_i8_kernel<kBf16, kQG>, threads, smem) != cudaSuccess ||
         n <= 0) {
       cudaGetLastError();
       n = 1;
@@ -1095,12 +1135,13 @@ int prepare_i8(int smem, int* blocks) {
 int launch_decode_i8(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
   const int qg = i8_groups(a, plan);
   const Layout L = i8_layout(a.d_boost, qg);
-  const int warps = i8_warps(qg);
+  const int warps = i8_warps(qg, a.d_boost);
   const int smem = warps * L.size;
   const bool bf16 = a.dtype == KITTY_DTYPE_BF16;
   int occ_blocks = 1;
-  const int rc = qg == 1 ? (bf16 ? prepare_i8<true, 1>(smem, &occ_blocks) : prepare_i8<false, 1>(smem, &occ_blocks))
-                         : (bf16 ? prepare_i8<true, 2>(smem, &occ_blocks) : prepare_i8<false, 2>(smem, &occ_blocks));
+  const int th = 32 * warps;
+  const int rc = qg == 1 ? (bf16 ? prepare_i8<true, 1>(th, smem, &occ_blocks) : prepare_i8<false, 1>(th, smem, &occ_blocks))
+                         : (bf16 ? prepare_i8<true, 2>(th, smem, &occ_blocks) : prepare_i8<false, 2>(th, smem, &occ_blocks));
   if (rc != KITTY_OK) return rc;
   int dev = 0, sms = 148;
   if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {

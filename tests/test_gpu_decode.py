@@ -135,6 +135,7 @@ def variant(request):
     (104, 2, 16, 2, [32 + 64 * 128 + 10, 40], 0.25),
     (105, 3, 48, 8, [32 + 5 * 128 + 17, 32 + 12 * 128, 90], 0.125),                        # 6 q heads per KV head
     (106, 2, 40, 8, [32 + 7 * 128 + 100, 32 + 128 + 1], 0.25),                             # 5 q heads per KV head
+    (107, 2, 64, 8, [32 + 8 * 128 + 9, 32 + 3 * 128 + 120], 0.5),    # 8:1, K=64: fewer warps per CTA
 ])
 def test_random_batches_vs_oracle(seed, B, Hq, H, ctx, rate, variant):
     case = synthetic.make_decode_case(seed, B, Hq, H, 128, ctx, boost_rate=rate)
