@@ -968,6 +968,10 @@ decode_i8_kernel(const KittyDecodeArgs a, DecodePlan plan) {
                 }
               }
             }
+            if (half == 1) {   // the value buffer has been read: request the next page's values
+              next_values();
+              v_requested = true;
+            }
 #pragma unroll
             for (int qg = 0; qg < kQG; ++qg)
 #pragma unroll
