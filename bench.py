@@ -219,7 +219,7 @@ def _kv(spec, b, T, heads, device, seed):
     """fp16 keys and values (H_local, T, D) of sequence ``b``: one generator per
     (sequence, KV head), so a shard builds exactly its part of the full workload."""
     import torch
-    from kitty import synthetic
+    import synthetic
     ks, vs = [], []
     for h in range(*heads):
         gen = torch.Generator(device=device)
@@ -439,7 +439,7 @@ def cpu_sample(spec, n_seq, seed=11):
     independent (sequence, KV head) units; returns (units, algorithmic bytes, label)."""
     import numpy as np
     sys.path.insert(0, str(ROOT))
-    from kitty import synthetic
+    import synthetic
     from oracle import kitty_oracle as O
     lay = sequence_layout(spec)[:n_seq]
     n_seq = len(lay)

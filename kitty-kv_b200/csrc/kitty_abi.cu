@@ -53,8 +53,10 @@ int validate_decode(const KittyDecodeArgs* a) {
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: dtype must be KITTY_DTYPE_F16 or KITTY_DTYPE_BF16");
   if (a->sink_len_all < 0 || a->tail_len_all < 0)
     return fail(KITTY_ERR_INVALID_ARGUMENT, "paged_decode: negative region length");
-  if (!simt_supports(*a))
-    return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: head_dim > 256 or more than 16 query heads per KV head");
+  if (!simt_supports(*a) && !i8_supports(*a))
+    return fail(KITTY_ERR_UNSUPPORTED,
+                "paged_decode: no kernel for this shape (the CUDA-core kernel takes head_dim <= 256 and at most 16 "
+                "query heads per KV head; the integer kernel head_dim = group = 128 with 16-byte aligned tensors)");
   return KITTY_OK;
 }
 
@@ -63,7 +65,7 @@ int choose_variant(const KittyDecodeArgs* a) {
   const int forced = g_forced_variant.load();
   if (forced == 3 && tc_supports(*a)) return 3;
   if (forced == 2 && i8_supports(*a)) return 2;
-  if (forced == 0) return 0;
+  if (forced == 0 && simt_supports(*a)) return 0;
   if (i8_supports(*a)) return 2;
   return 0;
 }

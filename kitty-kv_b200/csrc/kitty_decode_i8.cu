@@ -1044,7 +1044,7 @@ bool i8_supports(const KittyDecodeArgs& a) {
   auto region_ok = [](const void* p, int64_t s_seq, int64_t s_head, int64_t s_tok) {
     return p == nullptr || (aligned(p, 16) && s_seq % 8 == 0 && s_head % 8 == 0 && s_tok % 8 == 0);
   };
-  return a.head_dim == kD && a.group == kG && g >= 1 && g <= 2 * kI8MaxHeadsPerPass && a.d_boost <= 128 &&
+  return a.head_dim == kD && a.group == kG && g >= 1 && a.d_boost <= 128 &&
          aligned(a.q, 16) && a.q_s_seq % 8 == 0 && a.q_s_head % 8 == 0 &&
          region_ok(a.sink_k, a.sk_s_seq, a.sk_s_head, a.sk_s_tok) &&
          region_ok(a.sink_v, a.sv_s_seq, a.sv_s_head, a.sv_s_tok) &&

@@ -14,7 +14,7 @@ run, and the results are written next to this script:
   attention outputs for those cases.
 
 The GPU tests regenerate the 128-channel inputs from the recorded seeds with
-``kitty.synthetic`` (numpy PCG64, identical bytes everywhere), run the CUDA
+``synthetic`` (numpy PCG64, identical bytes everywhere), run the CUDA
 kernels and compare against these hashes/outputs; the CPU tests check that the
 numpy oracle reproduces every recorded reference output.
 """
@@ -37,7 +37,8 @@ import torch
 HERE = Path(__file__).resolve().parent
 REPO = HERE.parent.parent
 sys.path.insert(0, str(REPO / "kitty-kv_b200"))
-from kitty import synthetic  # noqa: E402  (numpy-only module of the drop-in package)
+sys.path.insert(0, str(REPO))
+import synthetic  # noqa: E402  (numpy-only input generator at the repository root)
 
 
 def sha(a: np.ndarray) -> str:

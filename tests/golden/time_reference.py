@@ -32,7 +32,7 @@ sys.path.insert(0, str(REPO))
 sys.path.insert(0, str(HERE))
 
 import make_golden as MG  # noqa: E402
-from kitty import synthetic  # noqa: E402
+import synthetic  # noqa: E402
 from oracle import kitty_oracle as O  # noqa: E402
 
 

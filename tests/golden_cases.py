@@ -2,7 +2,7 @@
 
 The manifest written by ``tests/golden/make_golden.py`` stores only seeds and
 shapes for the 128-channel cases; these helpers regenerate the exact inputs
-with ``kitty.synthetic`` (and check their hashes) so both the numpy oracle
+with ``synthetic`` (and check their hashes) so both the numpy oracle
 (CPU tests) and the CUDA kernels (GPU tests) can be compared against the
 reference's recorded outputs.
 """
@@ -11,7 +11,7 @@ from __future__ import annotations
 
 import numpy as np
 
-from kitty import synthetic
+import synthetic
 
 from conftest import sha
 

@@ -77,7 +77,7 @@ def _cpu_workload():
     tensors, with pools quantised by the oracle (permuted physical pages, ragged tails)."""
     import numpy as np
     import torch
-    from kitty import synthetic
+    import synthetic
     from oracle import kitty_oracle as O
     case = synthetic.make_decode_case(3, 3, 16, 4, 128, [32 + 5 * 128 + 7, 32 + 2 * 128, 32 + 3 * 128 + 100],
                                       tails=[7, 0, 100])

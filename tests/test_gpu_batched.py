@@ -17,7 +17,7 @@ import pytest
 import torch
 
 from kitty import BatchedKVCache, KittyConfig
-from kitty import synthetic
+import synthetic
 from kitty.kernels import _lib
 from oracle import kitty_oracle as O
 

@@ -16,7 +16,7 @@ import torch
 
 from kitty import BatchedKVCache, KittyConfig
 from kitty import kernels as KK
-from kitty import synthetic
+import synthetic
 from oracle import kitty_oracle as O
 
 from conftest import meta_by_value, sha

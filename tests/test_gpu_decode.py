@@ -14,7 +14,7 @@ import pytest
 import torch
 
 from kitty import kernels as KK
-from kitty import synthetic
+import synthetic
 from oracle import kitty_oracle as O
 
 import golden_cases as GC
@@ -257,6 +257,27 @@ def test_integer_family_beyond_eight_query_heads(hq, rate, splits):
         got = run_batched(case, pools, phys_of, num_splits=splits)
     finally:
         KK._lib.force_decode_variant(prev)
+    assert KK._lib.device_error_flags() == 0
+    exp = O.paged_attention_batched(case.q, bt, npg, tuple(p.cpu().numpy() for p in pools), case.boost_idx,
+                                    case.d_boost, sk, sv, sl, tk, tv, tl)
+    assert_close(got, exp)
+
+
+@pytest.mark.parametrize("hq,H,rate", [(48, 1, 0.125), (64, 2, 0.25), (40, 1, 0.125)])
+def test_multi_query_shapes_vs_oracle(hq, H, rate):
+    """Multi-query and wide-group shapes (48 query heads on one KV head, 32 per KV head,
+    40 on one): beyond the CUDA-core kernel's 16 query heads per KV head, so the integer
+    kernel runs them in passes of 8; the library's default choice must agree with the
+    oracle on a mixed batch with sinks, ragged tails and permuted pages."""
+    ctx = [32 + 5 * 128 + 77, 32 + 2 * 128, 100]
+    case = synthetic.make_decode_case(500 + hq + H, len(ctx), hq, H, 128, ctx, boost_rate=rate)
+    total = sum(s.n_pages for s in case.seqs)
+    n_phys = total + 3
+    phys_of = GC.phys_layout(case, 501, n_phys)
+    pools = build_pools_gpu(case, phys_of, n_phys)
+    sk, sv, sl, tk, tv, tl = GC.padded_regions(case)
+    bt, npg = GC.block_table(case, phys_of)
+    got = run_batched(case, pools, phys_of)
     assert KK._lib.device_error_flags() == 0
     exp = O.paged_attention_batched(case.q, bt, npg, tuple(p.cpu().numpy() for p in pools), case.boost_idx,
                                     case.d_boost, sk, sv, sl, tk, tv, tl)

@@ -23,7 +23,7 @@ import torch
 import kitty
 from kitty import KittyAttentionFactory, KittyConfig
 from kitty import kernels as KK
-from kitty import synthetic
+import synthetic
 from oracle import kitty_oracle as O
 
 from conftest import meta_by_value, sha

@@ -9,7 +9,7 @@ import pytest
 import torch
 
 from kitty import kernels as KK
-from kitty import synthetic
+import synthetic
 from oracle import kitty_oracle as O
 
 from conftest import meta_by_value, sha

@@ -154,7 +154,7 @@ def test_sequence_state_matches_reference_pipeline(golden_npz, golden_manifest, 
     count, the key pool bytes and the fp16 sink / Key Q-buffer contents.  (Value pages
     are not compared: the reference quantises its value window's evictions, the
     batched cache the values of the page's own tokens.)"""
-    from kitty import synthetic
+    import synthetic
     e = golden_manifest["pipeline"][name]
     cfg = e["config"]
     H, D, G, S = cfg["num_kv_heads"], cfg["head_dim"], cfg["q_buffer_size"], cfg["sink_size"]

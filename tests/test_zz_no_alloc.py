@@ -21,7 +21,7 @@ import numpy as np
 import pytest
 import torch
 
-from kitty import synthetic
+import synthetic
 from kitty.kernels import _lib
 
 pytestmark = pytest.mark.gpu
