@@ -143,6 +143,59 @@ def run_small(ref, rng, store):
     return names
 
 
+def nonfinite_cases():
+    """Key and value pages holding +-inf and NaN, small and D = G = 128 (their own
+    generator, so every other set keeps its bytes).  A channel (key) or token (value)
+    that holds one becomes a non-finite range and scale in the reference."""
+    rng = np.random.default_rng(2026)
+    keys = []
+    k = rng.standard_normal((16, 8)).astype(np.float16)
+    k[1, 2] = np.inf; k[5, 0] = -np.inf; k[6, 3] = np.nan; k[12, :] = np.inf
+    b = np.full(16, 5, np.uint8); b[[1, 6, 9, 13]] = np.arange(4)
+    keys.append(("nonfinite", k, b, 4, 5))
+    k = rng.standard_normal((128, 128)).astype(np.float16)
+    k[3, 5] = np.inf; k[10, 7] = -np.inf; k[20, 9] = np.nan; k[30, :] = np.inf; k[40, 11] = 60000.0
+    k[50, 3] = np.nan; k[50, 4] = np.inf
+    boosted = [3, 20, 50] + [c for c in rng.permutation(128).tolist() if c not in (3, 20, 50)][:13]
+    b = np.full(128, 17, np.uint8); b[boosted] = np.arange(16)
+    keys.append(("nonfinite_d128", k, b, 16, 17))
+    values = []
+    v = rng.standard_normal((8, 16)).astype(np.float16)
+    v[1, 2] = np.inf; v[3, 0] = np.nan; v[6, :] = -np.inf
+    values.append(("nonfinite", v))
+    v = rng.standard_normal((128, 128)).astype(np.float16)
+    v[2, 5] = np.inf; v[9, :] = -np.inf; v[17, 3] = np.nan; v[33, 0] = 65504.0; v[60, 1] = -np.inf
+    values.append(("nonfinite_d128", v))
+    return keys, values
+
+
+def run_nonfinite_sets(ref, store, manifest):
+    from kitty_ref.kernels import (quantize_key_page_torch, quantize_value_page_torch,
+                                   dequantize_key_page_torch, dequantize_value_page_torch)
+    keys, values = nonfinite_cases()
+    for name, key, bidx, K, sent in keys:
+        t2b, thi, sc, zp = quantize_key_page_torch(torch.from_numpy(key), torch.from_numpy(bidx), K, sent)
+        rec = dequantize_key_page_torch(t2b, thi, sc, zp, torch.from_numpy(bidx), K)
+        p = f"key/{name}/"
+        store[p + "key"] = key
+        store[p + "boost_idx"] = bidx
+        store[p + "params"] = np.array([K, sent], np.int64)
+        store[p + "low"] = t2b.numpy(); store[p + "high"] = thi.numpy()
+        store[p + "scale"] = sc.numpy(); store[p + "zero"] = zp.numpy()
+        store[p + "dequant"] = rec.numpy()
+        if ["key", name] not in manifest["small"]:
+            manifest["small"].append(["key", name])
+    for name, val in values:
+        pk, sc, zp = quantize_value_page_torch(torch.from_numpy(val))
+        rec = dequantize_value_page_torch(pk, sc, zp)
+        p = f"value/{name}/"
+        store[p + "value"] = val
+        store[p + "codes"] = pk.numpy(); store[p + "scale"] = sc.numpy(); store[p + "zero"] = zp.numpy()
+        store[p + "dequant"] = rec.numpy()
+        if ["value", name] not in manifest["small"]:
+            manifest["small"].append(["value", name])
+
+
 def build_pools_ref(ref, case: synthetic.DecodeCase, phys_of, n_phys):
     """Quantise every page-head of ``case`` with the reference into pools of
     ``n_phys`` pages; sequence b's page i goes to physical page phys_of[b][i]."""
@@ -456,9 +509,19 @@ def main():
     ap.add_argument("--skip-quant", action="store_true")
     ap.add_argument("--bf16-only", action="store_true",
                     help="add the bfloat16 sets to the existing golden files and keep everything else")
+    ap.add_argument("--nonfinite-only", action="store_true",
+                    help="add the non-finite key / value pages to the existing golden files")
     args = ap.parse_args()
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = load_reference(Path(args.reference))
+    if args.nonfinite_only:
+        with np.load(HERE / "golden_small.npz") as z:
+            store = {k: z[k] for k in z.files}
+        manifest = json.loads((HERE / "golden_manifest.json").read_text())
+        run_nonfinite_sets(ref, store, manifest)
+        np.savez_compressed(HERE / "golden_small.npz", **store)
+        (HERE / "golden_manifest.json").write_text(json.dumps(manifest, indent=1, default=int))
+        return
     if args.bf16_only:
         with np.load(HERE / "golden_small.npz") as z:
             store = {k: z[k] for k in z.files}
@@ -471,7 +534,8 @@ def main():
     store = {}
     manifest = {"generator": "tests/golden/make_golden.py", "torch": torch.__version__,
                 "numpy": np.__version__, "attention": {}, "pipeline": {}, "quant": {}}
-    manifest["small"] = run_small(ref, rng, store)
+    manifest["small"] = [list(x) for x in run_small(ref, rng, store)]
+    run_nonfinite_sets(ref, store, manifest)
     run_attention_sets(ref, store, manifest)
     run_pipeline_compat(ref, store, manifest)
     check_profiler(ref, manifest)

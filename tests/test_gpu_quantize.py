@@ -19,9 +19,10 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda:0"
 
 KEY_CASES = ["rand0", "rand1", "rand2", "rand3", "constant_channels", "all_zero", "wide_ranges",
-             "permuted_boost", "duplicate_rows", "boost_eq_k", "known_answer_0123", "halfway", "d128_page"]
+             "permuted_boost", "duplicate_rows", "boost_eq_k", "known_answer_0123", "halfway", "d128_page",
+             "nonfinite", "nonfinite_d128"]
 VALUE_CASES = ["rand0", "rand1", "rand2", "constant_3", "all_zero", "constant_rows", "wide_ranges",
-               "halfway", "d128_page"]
+               "halfway", "d128_page", "nonfinite", "nonfinite_d128"]
 
 
 def cuda(a):
@@ -163,6 +164,41 @@ def test_config3_sample_bit_exact(golden_manifest):
         assert sha(vc.cpu().numpy()) == ref["val_codes"]
         assert sha(vm[..., 0].cpu().numpy()) == ref["val_scale"]
         assert sha(meta_by_value(vm[..., 1].cpu().numpy())) == ref["val_zero_value"]
+
+
+def test_nonfinite_pages_on_the_token_major_path(golden_npz):
+    """The D = G = 128 page quantisers (token-major source, batched entry points: the path
+    a cache flush and a prefill take) on pages holding +-inf and NaN: channels (keys) and
+    tokens (values) with a non-finite range take the exact per-element path and must
+    still equal the reference's recorded pages byte for byte (metadata by value)."""
+    pk, pv = "key/nonfinite_d128/", "value/nonfinite_d128/"
+    key, bidx = golden_npz[pk + "key"], golden_npz[pk + "boost_idx"]
+    K, sent = (int(x) for x in golden_npz[pk + "params"])
+    D, G = key.shape
+    H, S = 1, 32
+    # (H, T, D) caches: S leading tokens, then the page
+    kt = torch.zeros(H, S + G, D, dtype=torch.float16, device=DEV)
+    kt[0, S:] = cuda(np.ascontiguousarray(key.T))
+    vt = torch.zeros(H, S + G, D, dtype=torch.float16, device=DEV)
+    vt[0, S:] = cuda(golden_npz[pv + "value"])
+    offs = torch.tensor([S * D], dtype=torch.int64, device=DEV)
+    dst = torch.tensor([1], dtype=torch.int32, device=DEV)
+    kl = torch.zeros(2, H, D, G // 4, dtype=torch.uint8, device=DEV)
+    kh = torch.zeros(2, H, K, G // 4, dtype=torch.uint8, device=DEV)
+    km = torch.zeros(2, H, 2, D, dtype=torch.float16, device=DEV)
+    vc = torch.zeros(2, H, G, D // 4, dtype=torch.uint8, device=DEV)
+    vm = torch.zeros(2, H, G, 2, dtype=torch.float16, device=DEV)
+    KK.quantize_key_pages(kt, offs, tuple(kt.stride()), cuda(bidx[None, :]), K, sent, dst, kl, kh, km, H, D, G)
+    KK.quantize_value_pages(vt, offs, tuple(vt.stride()), dst, vc, vm, H, D, G)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(kl[1, 0].cpu().numpy(), golden_npz[pk + "low"])
+    np.testing.assert_array_equal(kh[1, 0].cpu().numpy(), golden_npz[pk + "high"])
+    np.testing.assert_array_equal(meta_by_value(km[1, 0, 0].cpu().numpy()), meta_by_value(golden_npz[pk + "scale"]))
+    np.testing.assert_array_equal(meta_by_value(km[1, 0, 1].cpu().numpy()), meta_by_value(golden_npz[pk + "zero"]))
+    np.testing.assert_array_equal(vc[1, 0].cpu().numpy(), golden_npz[pv + "codes"])
+    np.testing.assert_array_equal(meta_by_value(vm[1, 0, :, 0].cpu().numpy()), meta_by_value(golden_npz[pv + "scale"]))
+    np.testing.assert_array_equal(meta_by_value(vm[1, 0, :, 1].cpu().numpy()), meta_by_value(golden_npz[pv + "zero"]))
+    assert (kl[0] == 0).all() and (vc[0] == 0).all()
 
 
 def test_value_partial_buffer_zero_padding():

@@ -15,7 +15,7 @@ import golden_cases as GC
 
 @pytest.mark.parametrize("name", ["rand0", "rand1", "rand2", "rand3", "constant_channels", "all_zero",
                                   "wide_ranges", "permuted_boost", "duplicate_rows", "boost_eq_k",
-                                  "known_answer_0123", "halfway", "d128_page"])
+                                  "known_answer_0123", "halfway", "d128_page", "nonfinite", "nonfinite_d128"])
 def test_key_quantize_matches_reference(golden_npz, name):
     p = f"key/{name}/"
     K, sent = (int(x) for x in golden_npz[p + "params"])
@@ -29,12 +29,12 @@ def test_key_quantize_matches_reference(golden_npz, name):
 
 
 def test_every_small_case_is_covered(golden_npz):
-    assert len(small_case_names(golden_npz, "key")) == 13
-    assert len(small_case_names(golden_npz, "value")) == 9
+    assert len(small_case_names(golden_npz, "key")) == 15
+    assert len(small_case_names(golden_npz, "value")) == 11
 
 
 @pytest.mark.parametrize("name", ["rand0", "rand1", "rand2", "constant_3", "all_zero", "constant_rows",
-                                  "wide_ranges", "halfway", "d128_page"])
+                                  "wide_ranges", "halfway", "d128_page", "nonfinite", "nonfinite_d128"])
 def test_value_quantize_matches_reference(golden_npz, name):
     p = f"value/{name}/"
     codes, sc, zp = O.quantize_value_page(golden_npz[p + "value"])
