@@ -49,27 +49,27 @@ ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT / "kitty-kv_b200"))
 
 METRIC = "quantized paged decode-attn HBM GB/s (% of peak) & tokens/s at 1/2/4/8 B200"
-# DRAM bytes (read + write) of one decode launch, from one ncu capture
-# (dram__bytes_read.sum + dram__bytes_write.sum) of this script on the same workload
-# and kernel; None where no capture exists.  Config 4 was captured at batch 8
-# (`--batch 8`, 1/8 of the page-heads) and scaled by 8: its traffic is per page-head.
+# DRAM bytes (read + write) of one decode launch per algorithmic byte, from one ncu
+# capture (dram__bytes_read.sum + dram__bytes_write.sum) of this script on the same
+# workload and kernel: (captured traffic, algorithmic bytes of the captured launch).
+# Every page-head is read once, so the ratio carries over to other batch sizes and to
+# each rank's share.  Config 2 was captured at full size, config 4 at `--batch 8`,
+# config 5 at `--batch 32` (its first 32 sequences).
 MEASURED_TRAFFIC = {
-    ("config2", "decode_i8_kernel"): 652_503_552 + 4_320_256,
-    ("config4", "decode_i8_kernel"): (641_750_016 + 4_122_624) * 8,
+    ("config2", "decode_i8_kernel"): (652_503_552 + 4_320_256, 652_377_984),
+    ("config4", "decode_i8_kernel"): (642_340_352 + 8_742_912, 641_400_800),
+    ("config5", "decode_i8_kernel"): (624_861_952 + 4_979_200, 624_760_012),
 }
 
-def measured_traffic(workload, kernel, world):
-    """Captured DRAM bytes of one decode launch on this rank: the single-GPU capture,
-    divided among the ranks for the workloads whose ranks split one job's page-heads
-    evenly (config 4's KV heads); None where the split is uneven or no capture exists."""
+
+def measured_traffic(workload, kernel, nbytes, pages_only=False):
+    """DRAM bytes of one decode launch on this rank moving `nbytes` algorithmic bytes,
+    scaled from the capture; None where no capture of this workload and kernel exists
+    (and for the pages-only form, which the captures do not cover)."""
     t = MEASURED_TRAFFIC.get((workload, kernel))
-    if t is None or world == 1:
-        return t
-    if WORKLOADS[workload].get("shard") == "replica":
-        return t
-    if WORKLOADS[workload].get("shard") == "kv_head":
-        return t // world
-    return None
+    if t is None or pages_only:
+        return None
+    return int(round(t[0] / t[1] * nbytes))
 
 
 WORKLOADS = {
@@ -789,7 +789,7 @@ def decode_arm(args, spec, d, device, local):
         "e2e": {"value": round(nbytes_total / (e2e_ms * 1e-3) / 1e9, 2), "unit": "GB/s",
                 "ms_per_step": round(e2e_ms, 4), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
         "roofline": {"bound": "hbm", "achieved": round(achieved, 2), "peak": peak, "unit": "GB/s",
-                     "frac": round(achieved / peak, 4), "traffic": measured_traffic(args.workload, kernel, world),
+                     "frac": round(achieved / peak, 4), "traffic": measured_traffic(args.workload, kernel, nbytes_local, w["pages_only"]),
                      "peak_source": f"{peak_kind} copy bandwidth", "kernel": f"{kernel} (+ split merge)",
                      "algorithmic_bytes_per_launch": nbytes_local},
         "cpu_baseline": cpu,
