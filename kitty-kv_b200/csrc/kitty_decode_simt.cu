@@ -23,7 +23,7 @@ constexpr int kMaxGroupSimt = 16;  // query heads per KV head
 
 struct SimtSmem {
   // offsets into dynamic shared memory (bytes)
-  size_t q, kl, kh, km, vc, vm, p, row, red, stats, total;
+  size_t q, kl, kh, vc, ks, kz, vs, vz, p, row, red, stats, total;
 };
 
 __host__ __device__ inline SimtSmem simt_layout(int D, int G, int K, int g) {
@@ -33,9 +33,11 @@ __host__ __device__ inline SimtSmem simt_layout(int D, int G, int K, int g) {
   s.q = take(size_t(g) * D * 4);
   s.kl = take(size_t(D) * (G / 4));
   s.kh = take(size_t(K) * (G / 4) + 4);
-  s.km = take(size_t(2) * D * 2);
   s.vc = take(size_t(G) * (D / 4));
-  s.vm = take(size_t(G) * 2 * 2);
+  s.ks = take(size_t(D) * 4);   // key scale / zero-point per channel, float
+  s.kz = take(size_t(D) * 4);
+  s.vs = take(size_t(G) * 4);   // value scale / zero-point per token, float
+  s.vz = take(size_t(G) * 4);
   const int chunk = G > kSimtThreads ? G : kSimtThreads;
   s.p = take(size_t(g) * chunk * 4);
   s.row = take(size_t(D) * 4);
@@ -45,7 +47,20 @@ __host__ __device__ inline SimtSmem simt_layout(int D, int G, int K, int g) {
   return s;
 }
 
-template <bool kBf16>
+// bytes [0, n) of src into dst: 16-byte copies when both ends allow it
+__device__ __forceinline__ void stage_bytes(uint8_t* dst, const uint8_t* src, int n, int tid) {
+  if (((reinterpret_cast<uintptr_t>(src) | reinterpret_cast<uintptr_t>(dst)) & 15) == 0 && (n & 15) == 0) {
+    for (int i = tid; i < n / 16; i += kSimtThreads)
+      reinterpret_cast<uint4*>(dst)[i] = reinterpret_cast<const uint4*>(src)[i];
+  } else {
+    for (int i = tid; i < n; i += kSimtThreads) dst[i] = src[i];
+  }
+}
+
+// kGT: query heads per KV head rounded up to a power of two (loops over heads have a
+// constant trip count; heads g .. kGT-1 are predicated off).  Channels and tokens of
+// the inner loops go four at a time: q, probabilities and metadata as 16-byte loads.
+template <bool kBf16, int kGT>
 __global__ void __launch_bounds__(kSimtThreads)
 decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   using T = Half16<kBf16>;
@@ -60,9 +75,11 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   float* q_s = reinterpret_cast<float*>(smem + L.q);
   uint8_t* kl_s = smem + L.kl;
   uint8_t* kh_s = smem + L.kh;
-  uint16_t* km_s = reinterpret_cast<uint16_t*>(smem + L.km);
   uint8_t* vc_s = smem + L.vc;
-  uint16_t* vm_s = reinterpret_cast<uint16_t*>(smem + L.vm);
+  float* ks_s = reinterpret_cast<float*>(smem + L.ks);
+  float* kz_s = reinterpret_cast<float*>(smem + L.kz);
+  float* vs_s = reinterpret_cast<float*>(smem + L.vs);
+  float* vz_s = reinterpret_cast<float*>(smem + L.vz);
   float* p_s = reinterpret_cast<float*>(smem + L.p);
   int* row_s = reinterpret_cast<int*>(smem + L.row);
   float* red_s = reinterpret_cast<float*>(smem + L.red);
@@ -85,11 +102,11 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
 
   // per-thread accumulators: channel c = tid + j*128 for j < ceil(D/128)
   constexpr int kMaxChanPerThread = 2;  // D <= 256
-  float o_acc[kMaxChanPerThread][kMaxGroupSimt];
+  float o_acc[kMaxChanPerThread][kGT];
 #pragma unroll
   for (int j = 0; j < kMaxChanPerThread; ++j)
 #pragma unroll
-    for (int qh = 0; qh < kMaxGroupSimt; ++qh) o_acc[j][qh] = 0.f;
+    for (int qh = 0; qh < kGT; ++qh) o_acc[j][qh] = 0.f;
 
   const int cr = a.seq_map ? a.seq_map[b] : b;   // cache row of batch row b
   const int npages = a.num_pages[cr];
@@ -111,55 +128,67 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       page = a.block_table[cr * a.bt_s_seq + p_begin + (item - fp16_chunks)];
       if (page < 0 || page >= a.pool_pages) continue;  // out-of-range entries are skipped
       ntok = G;
-      // stage the five pool slices
-      const uint8_t* kl = a.key_low + (page * H + h) * (int64_t(D) * (G / 4));
-      const uint8_t* kh = a.key_high + (page * H + h) * (int64_t(K) * (G / 4));
-      const uint16_t* km = reinterpret_cast<const uint16_t*>(a.key_meta) + (page * H + h) * (2 * int64_t(D));
-      const uint8_t* vc = a.val_codes + (page * H + h) * (int64_t(G) * (D / 4));
-      const uint16_t* vm = reinterpret_cast<const uint16_t*>(a.val_meta) + (page * H + h) * (2 * int64_t(G));
-      for (int i = tid; i < D * (G / 4); i += kSimtThreads) kl_s[i] = kl[i];
-      for (int i = tid; i < K * (G / 4); i += kSimtThreads) kh_s[i] = kh[i];
-      for (int i = tid; i < 2 * D; i += kSimtThreads) km_s[i] = km[i];
-      for (int i = tid; i < G * (D / 4); i += kSimtThreads) vc_s[i] = vc[i];
-      for (int i = tid; i < 2 * G; i += kSimtThreads) vm_s[i] = vm[i];
+      // stage the code planes; metadata straight to float
+      const int64_t ph = page * H + h;
+      stage_bytes(kl_s, a.key_low + ph * (int64_t(D) * (G / 4)), D * (G / 4), tid);
+      stage_bytes(kh_s, a.key_high + ph * (int64_t(K) * (G / 4)), K * (G / 4), tid);
+      stage_bytes(vc_s, a.val_codes + ph * (int64_t(G) * (D / 4)), G * (D / 4), tid);
+      const uint16_t* km = reinterpret_cast<const uint16_t*>(a.key_meta) + ph * (2 * int64_t(D));
+      const uint16_t* vm = reinterpret_cast<const uint16_t*>(a.val_meta) + ph * (2 * int64_t(G));
+      for (int c = tid; c < D; c += kSimtThreads) { ks_s[c] = T::to_f(km[c]); kz_s[c] = T::to_f(km[D + c]); }
+      for (int t = tid; t < G; t += kSimtThreads) { vs_s[t] = T::to_f(vm[2 * t]); vz_s[t] = T::to_f(vm[2 * t + 1]); }
     } else {
       f0 = item * chunk_cap;
       ntok = min(chunk_cap, fp16_tokens - f0);
     }
     __syncthreads();
 
-    // ---- scores: thread <-> token
+    // ---- scores: thread <-> token, channels four at a time
     for (int t = tid; t < chunk_cap; t += kSimtThreads) {
-      float acc[kMaxGroupSimt];
+      float acc[kGT];
 #pragma unroll
-      for (int qh = 0; qh < kMaxGroupSimt; ++qh) acc[qh] = 0.f;
+      for (int qh = 0; qh < kGT; ++qh) acc[qh] = 0.f;
       if (t < ntok) {
-        if (is_page) {
-          const int G4 = G / 4, j = t >> 2, sh = 2 * (t & 3);
-          for (int c = 0; c < D; ++c) {
-            uint32_t code = (kl_s[c * G4 + j] >> sh) & 3u;
-            const int r = row_s[c];
-            if (r >= 0) code |= ((kh_s[r * G4 + j] >> sh) & 3u) << 2;
-            const float kv = (static_cast<float>(code) - T::to_f(km_s[D + c])) * T::to_f(km_s[c]);
-#pragma unroll
-            for (int qh = 0; qh < kMaxGroupSimt; ++qh)
-              if (qh < g) acc[qh] = fmaf(q_s[qh * D + c], kv, acc[qh]);
-          }
-        } else {
+        const int G4 = G / 4, j = t >> 2, sh = 2 * (t & 3);
+        const uint16_t* kp = nullptr;
+        if (!is_page) {
           const int ft = f0 + t;
-          const uint16_t* kp = (ft < sink_len)
+          kp = (ft < sink_len)
               ? reinterpret_cast<const uint16_t*>(a.sink_k) + cr * a.sk_s_seq + h * a.sk_s_head + ft * a.sk_s_tok
               : reinterpret_cast<const uint16_t*>(a.tail_k) + cr * a.tk_s_seq + h * a.tk_s_head + (ft - sink_len) * a.tk_s_tok;
-          for (int c = 0; c < D; ++c) {
-            const float kv = T::to_f(kp[c]);
+        }
+        for (int c = 0; c < D; c += 4) {
+          float kv[4];
+          if (is_page) {
+            const int4 r4 = *reinterpret_cast<const int4*>(row_s + c);
+            const float4 s4 = *reinterpret_cast<const float4*>(ks_s + c);
+            const float4 z4 = *reinterpret_cast<const float4*>(kz_s + c);
+            const int rr[4] = {r4.x, r4.y, r4.z, r4.w};
+            const float ss[4] = {s4.x, s4.y, s4.z, s4.w}, zz[4] = {z4.x, z4.y, z4.z, z4.w};
 #pragma unroll
-            for (int qh = 0; qh < kMaxGroupSimt; ++qh)
-              if (qh < g) acc[qh] = fmaf(q_s[qh * D + c], kv, acc[qh]);
+            for (int i = 0; i < 4; ++i) {
+              uint32_t code = (kl_s[(c + i) * G4 + j] >> sh) & 3u;
+              if (rr[i] >= 0) code |= ((kh_s[rr[i] * G4 + j] >> sh) & 3u) << 2;
+              kv[i] = (static_cast<float>(code) - zz[i]) * ss[i];
+            }
+          } else {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) kv[i] = T::to_f(kp[c + i]);
+          }
+#pragma unroll
+          for (int qh = 0; qh < kGT; ++qh) {
+            if (qh < g) {
+              const float4 qv = *reinterpret_cast<const float4*>(q_s + qh * D + c);
+              acc[qh] = fmaf(qv.x, kv[0], acc[qh]);
+              acc[qh] = fmaf(qv.y, kv[1], acc[qh]);
+              acc[qh] = fmaf(qv.z, kv[2], acc[qh]);
+              acc[qh] = fmaf(qv.w, kv[3], acc[qh]);
+            }
           }
         }
       }
 #pragma unroll
-      for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+      for (int qh = 0; qh < kGT; ++qh)
         if (qh < g) p_s[qh * chunk_cap + t] = (t < ntok) ? acc[qh] * a.sm_scale : -INFINITY;
     }
     __syncthreads();
@@ -200,22 +229,33 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
       l_s[tid] = l_s[tid] * alpha_s[tid] + sum;
     }
 
-    // ---- accumulate: thread <-> channel
+    // ---- accumulate: thread <-> channel; page tokens four at a time
 #pragma unroll
     for (int j = 0; j < kMaxChanPerThread; ++j) {
       const int c = tid + j * kSimtThreads;
       if (c >= D) break;
-      float acc[kMaxGroupSimt];
+      float acc[kGT];
 #pragma unroll
-      for (int qh = 0; qh < kMaxGroupSimt; ++qh) acc[qh] = o_acc[j][qh] * (qh < g ? alpha_s[qh] : 0.f);
+      for (int qh = 0; qh < kGT; ++qh) acc[qh] = o_acc[j][qh] * (qh < g ? alpha_s[qh] : 0.f);
       if (is_page) {
         const int D4 = D / 4, jj = c >> 2, sh = 2 * (c & 3);
-        for (int t = 0; t < ntok; ++t) {
-          const uint32_t code = (vc_s[t * D4 + jj] >> sh) & 3u;
-          const float vv = (static_cast<float>(code) - T::to_f(vm_s[2 * t + 1])) * T::to_f(vm_s[2 * t]);
+        for (int t = 0; t < ntok; t += 4) {
+          const float4 s4 = *reinterpret_cast<const float4*>(vs_s + t);
+          const float4 z4 = *reinterpret_cast<const float4*>(vz_s + t);
+          const float vv[4] = {(static_cast<float>((vc_s[t * D4 + jj] >> sh) & 3u) - z4.x) * s4.x,
+                               (static_cast<float>((vc_s[(t + 1) * D4 + jj] >> sh) & 3u) - z4.y) * s4.y,
+                               (static_cast<float>((vc_s[(t + 2) * D4 + jj] >> sh) & 3u) - z4.z) * s4.z,
+                               (static_cast<float>((vc_s[(t + 3) * D4 + jj] >> sh) & 3u) - z4.w) * s4.w};
 #pragma unroll
-          for (int qh = 0; qh < kMaxGroupSimt; ++qh)
-            if (qh < g) acc[qh] = fmaf(p_s[qh * chunk_cap + t], vv, acc[qh]);
+          for (int qh = 0; qh < kGT; ++qh) {
+            if (qh < g) {
+              const float4 pv = *reinterpret_cast<const float4*>(p_s + qh * chunk_cap + t);
+              acc[qh] = fmaf(pv.x, vv[0], acc[qh]);
+              acc[qh] = fmaf(pv.y, vv[1], acc[qh]);
+              acc[qh] = fmaf(pv.z, vv[2], acc[qh]);
+              acc[qh] = fmaf(pv.w, vv[3], acc[qh]);
+            }
+          }
         }
       } else {
         for (int t = 0; t < ntok; ++t) {
@@ -225,12 +265,12 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
               : reinterpret_cast<const uint16_t*>(a.tail_v) + cr * a.tv_s_seq + h * a.tv_s_head + (ft - sink_len) * a.tv_s_tok;
           const float vv = T::to_f(vp[c]);
 #pragma unroll
-          for (int qh = 0; qh < kMaxGroupSimt; ++qh)
+          for (int qh = 0; qh < kGT; ++qh)
             if (qh < g) acc[qh] = fmaf(p_s[qh * chunk_cap + t], vv, acc[qh]);
         }
       }
 #pragma unroll
-      for (int qh = 0; qh < kMaxGroupSimt; ++qh) o_acc[j][qh] = acc[qh];
+      for (int qh = 0; qh < kGT; ++qh) o_acc[j][qh] = acc[qh];
     }
     __syncthreads();
   }
@@ -240,7 +280,9 @@ decode_simt_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   for (int j = 0; j < kMaxChanPerThread; ++j) {
     const int c = tid + j * kSimtThreads;
     if (c >= D) break;
-    for (int qh = 0; qh < g; ++qh) {
+#pragma unroll
+    for (int qh = 0; qh < kGT; ++qh) {
+      if (qh >= g) break;
       if (plan.num_splits == 1) {
         const float l = l_s[qh];
         uint16_t* out = reinterpret_cast<uint16_t*>(a.out) + b * a.out_s_seq + (h * g + qh) * a.out_s_head;
@@ -369,17 +411,30 @@ decode_merge_kernel(const KittyDecodeArgs a, DecodePlan plan) {
   }
 }
 
+namespace {
+template <bool kBf16, int kGT>
+void launch_simt_t(const KittyDecodeArgs& a, const DecodePlan& plan, size_t smem, cudaStream_t stream) {
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(decode_simt_kernel<kBf16, kGT>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(smem));
+  dim3 grid(plan.num_splits, a.num_kv_heads, a.batch);
+  decode_simt_kernel<kBf16, kGT><<<grid, kSimtThreads, smem, stream>>>(a, plan);
+}
+template <bool kBf16>
+void launch_simt_g(const KittyDecodeArgs& a, const DecodePlan& plan, size_t smem, int g, cudaStream_t stream) {
+  if (g <= 1) launch_simt_t<kBf16, 1>(a, plan, smem, stream);
+  else if (g <= 2) launch_simt_t<kBf16, 2>(a, plan, smem, stream);
+  else if (g <= 4) launch_simt_t<kBf16, 4>(a, plan, smem, stream);
+  else if (g <= 8) launch_simt_t<kBf16, 8>(a, plan, smem, stream);
+  else launch_simt_t<kBf16, 16>(a, plan, smem, stream);
+}
+}  // namespace
+
 int launch_decode_simt(const KittyDecodeArgs& a, const DecodePlan& plan, cudaStream_t stream) {
   const int g = a.num_q_heads / a.num_kv_heads;
   const SimtSmem L = simt_layout(a.head_dim, a.group, a.d_boost, g);
   if (L.total > 200 * 1024) return fail(KITTY_ERR_UNSUPPORTED, "paged_decode: shape needs too much shared memory");
-  if (L.total > 48 * 1024) {
-    cudaFuncSetAttribute(decode_simt_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
-    cudaFuncSetAttribute(decode_simt_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, int(L.total));
-  }
-  dim3 grid(plan.num_splits, a.num_kv_heads, a.batch);
-  if (a.dtype == KITTY_DTYPE_BF16) decode_simt_kernel<true><<<grid, kSimtThreads, L.total, stream>>>(a, plan);
-  else decode_simt_kernel<false><<<grid, kSimtThreads, L.total, stream>>>(a, plan);
+  if (a.dtype == KITTY_DTYPE_BF16) launch_simt_g<true>(a, plan, L.total, g, stream);
+  else launch_simt_g<false>(a, plan, L.total, g, stream);
   return check_launch("decode_simt_kernel");
 }
 
@@ -394,7 +449,7 @@ int launch_decode_merge(const KittyDecodeArgs& a, const DecodePlan& plan, cudaSt
 
 bool simt_supports(const KittyDecodeArgs& a) {
   const int g = a.num_q_heads / a.num_kv_heads;
-  return a.head_dim <= 256 && g <= kMaxGroupSimt;
+  return a.head_dim <= 256 && a.head_dim % 4 == 0 && a.group % 4 == 0 && g <= kMaxGroupSimt;
 }
 
 }  // namespace kitty
