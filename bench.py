@@ -644,17 +644,28 @@ def decode_arm(args, spec, d, device, local):
         # the decode writes this rank's heads head-major, (Hq_local, B, D), through the
         # output strides, straight into the buffer the all-gather sends; the gathered
         # (Hq, B, D) buffer needs no reordering either
-        from kitty.distributed import gather_head_outputs
+        from kitty.distributed import PeerGather, gather_head_outputs
         out_hm = torch.empty(Hq, B, D, dtype=torch.float16, device=device)
         out = out_hm.permute(1, 0, 2)
         full = torch.empty(world * Hq, B, D, dtype=torch.float16, device=device)
+        peer_gather = None
+        if args.gather == "p2p":   # direct NVLink stores into every rank's exchange region
+            try:
+                peer_gather = PeerGather(Hq, B, D, device=device)
+            except RuntimeError as e:   # raised on every rank alike: all fall back to NCCL
+                print(f"[bench] {e}; using the NCCL all-gather", file=sys.stderr)
+                args.gather = "nccl"
+        if peer_gather is not None:
+            gather_fn = lambda src, dst: peer_gather(src, full=dst)
+        else:                      # NCCL all_gather_into_tensor
+            gather_fn = lambda src, dst: gather_head_outputs(src, full=dst)
     else:
         out = torch.empty(B, Hq, D, dtype=torch.float16, device=device)
 
     def eager_step():
         decode_call(w, out=out)
         if gather:
-            gather_head_outputs(out_hm, full=full)
+            gather_fn(out_hm, full)
 
     for _ in range(args.warmup):
         eager_step()
@@ -693,7 +704,7 @@ def decode_arm(args, spec, d, device, local):
             step = g_step.replay
         except Exception as e:
             launch_mode += f"; all-gather eager ({type(e).__name__})"
-            step = lambda: (run_decode(), gather_head_outputs(out_hm, full=full))
+            step = lambda: (run_decode(), gather_fn(out_hm, full))
 
     for _ in range(args.warmup):
         step()
@@ -703,7 +714,7 @@ def decode_arm(args, spec, d, device, local):
     decode_ms, launch_ms = timed(stream, args.steps, run_decode, torch, device, d)
     gather_ms = None
     if gather:
-        gather_ms, _ = timed(stream, args.steps, lambda: gather_head_outputs(out_hm, full=full), torch, device, d)
+        gather_ms, _ = timed(stream, args.steps, lambda: gather_fn(out_hm, full), torch, device, d)
     step_out = full if gather else out      # the step's result: the gathered heads under TP
 
     # ---- end to end through the public API with host buffers: a step's inputs (q, block
@@ -733,7 +744,7 @@ def decode_arm(args, spec, d, device, local):
         q, bt, npg = (in_dev[at:at + n].view(dt).view(shape) for at, n, dt, shape in in_views)
         if gather:
             decode_call(w, q=q, bt=bt, npg=npg, out=e2e_hm.permute(1, 0, 2))
-            gather_head_outputs(e2e_hm, full=e2e_full)
+            gather_fn(e2e_hm, e2e_full)
             out_host.copy_(e2e_full, non_blocking=True)
         else:
             out_host.copy_(decode_call(w, q=q, bt=bt, npg=npg), non_blocking=True)
@@ -743,9 +754,20 @@ def decode_arm(args, spec, d, device, local):
     torch.cuda.synchronize(device)
     e2e_ms, _ = timed(stream, args.steps, e2e_step, torch, device, d)
     same = bool(torch.equal(step_out.cpu(), out_host))
+    gather_exact = None
+    if gather:
+        # the exchanged output against an NCCL all-gather of the same per-rank slices
+        ref_full = torch.empty_like(full)
+        d.dist.all_gather_into_tensor(ref_full, out_hm)
+        ok = torch.tensor([1 if torch.equal(ref_full, full) else 0], device=device)
+        d.dist.all_reduce(ok, op=d.dist.ReduceOp.MIN)
+        gather_exact = bool(ok.item())
+        same = same and gather_exact
     # graphs holding NCCL calls are released before the process group is destroyed
     step = run_decode = g_decode = g_step = None
     graphs.clear()
+    if gather and peer_gather is not None:
+        peer_gather.close()
     # the timed output against the oracle on sampled rows of this rank's batch
     check = None
     if rank == 0:
@@ -757,6 +779,8 @@ def decode_arm(args, spec, d, device, local):
                  "max_abs_err": round(abs_err, 6), "max_err_over_tol": round(ratio, 4),
                  "pass": bool(ratio <= 1.0) and same, "e2e_equals_device_resident": same,
                  "check_s": round(time.perf_counter() - t0, 2)}
+        if gather_exact is not None:
+            check["gathered_equals_nccl_all_gather"] = gather_exact
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -774,7 +798,9 @@ def decode_arm(args, spec, d, device, local):
            "tail": w["tail_len"] if isinstance(w["tail_len"], int) else "per sequence", "d_boost": K,
            "parallelism": ("single GPU" if world == 1 else
                            {"replica": f"sequence-sharded x{world} (own sequences per rank)",
-                            "kv_head": f"KV-head tensor parallel x{world} + NCCL all-gather of outputs",
+                            "kv_head": f"KV-head tensor parallel x{world} + " + (
+                                "peer-memory all-gather of outputs (NVLink stores, kitty_tp_allgather)"
+                                if args.gather == "p2p" else "NCCL all-gather of outputs"),
                             "sequence": f"sequences over {world} ranks by longest-processing-time"}[spec["shard"]]),
            "decode_kernel": kernel, "launch": launch_mode,
            "l2": "inputs larger than L2 (no flush)" if nbytes_local > 126e6 else
@@ -914,8 +940,11 @@ def main():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="config2")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--variant", choices=["auto", "simt", "int8", "tc"], default="auto",
-                    help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128 "
-                         "and up to 8 query heads per KV head, CUDA-core kernel otherwise)")
+                    help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128, "
+                         "CUDA-core kernel otherwise)")
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+                    help="tensor-parallel output exchange (config 4 on several GPUs): direct NVLink stores "
+                         "into every rank's exchange region, or an NCCL all-gather")
     ap.add_argument("--pages-only", action="store_true",
                     help="decode the quantised pages alone (no fp16 sink / tail tokens; the bytes count "
                          "the pages only): isolates the page path, and the only calls the tcgen05 family takes")

@@ -38,7 +38,7 @@ extern "C" {
 #define KITTY_ERR_CUDA 3             /* a CUDA runtime call failed */
 #define KITTY_ERR_WORKSPACE 4        /* workspace missing or too small */
 
-#define KITTY_ABI_VERSION 4
+#define KITTY_ABI_VERSION 5
 
 /* 16-bit floating-point type of the fp16 tensors of a call (the `dtype` field
  * of the argument structs; 0 = the zero-initialised default).  With bf16 the
@@ -67,7 +67,8 @@ const char* kitty_last_error(void);
 /* sizeof() of the argument structs below, so a foreign-function binding can
  * check its mirror of them: kind 0 = KittyKeyQuantArgs, 1 = KittyValueQuantArgs,
  * 2 = KittyKeyDequantArgs, 3 = KittyDecodeArgs, 4 = KittyCacheState,
- * 5 = KittyPrefillArgs, 6 = KittyValueDequantArgs; 0 for an unknown kind. */
+ * 5 = KittyPrefillArgs, 6 = KittyValueDequantArgs, 7 = KittyTpGatherArgs; 0 for an
+ * unknown kind. */
 size_t kitty_args_size(int kind);
 
 /* ---------------------------------------------------------------------------
@@ -398,9 +399,58 @@ int kitty_cache_release(const KittyCacheState* state, int32_t n, const int32_t* 
 /* Sticky error bits set by device code on the current device (bit 0: a decode
  * kernel gave up waiting for a bulk copy after its bounded wait and returned
  * without a valid result; bits 1-5: kitty_cache_append / _prefill / _release,
- * above).  Synchronises with the device; clear != 0 resets the bits after
- * reading them. */
+ * above; bit 6: kitty_tp_allgather gave up waiting for another rank).
+ * Synchronises with the device; clear != 0 resets the bits after reading them. */
 int kitty_device_error_flags(uint32_t* flags, int clear);
+
+/* ---------------------------------------------------------------------------
+ * Tensor-parallel output exchange over peer memory (no counterpart in the
+ * reference, which is single-GPU).  When the decode is sharded by KV head, rank r
+ * holds the head-major outputs of its query heads, (Hq_local, B, D) fp16, and
+ * every rank needs all of them, (Hq, B, D).  Instead of a library all-gather,
+ * each rank's exchange region (one cudaMalloc, mapped into the other ranks'
+ * processes by CUDA IPC) receives the slices by direct NVLink stores:
+ *
+ *   region = [buffer 0: data_bytes][buffer 1: data_bytes][arrival counters:
+ *             KITTY_TP_MAX_RANKS x u32][epoch u32][done u32]   (see
+ *             kitty_tp_region_bytes)
+ *
+ * kitty_tp_allgather launches two kernels on `stream`: the first stores this
+ * rank's slice (src_bytes at src) at byte offset dst_offset of buffer (e & 1)
+ * of every rank (e = the call's epoch, counted on the device, so CUDA-graph
+ * replays stay in step) and then adds to that rank's arrival counter for this
+ * rank (system-scope fence first); the second waits until every rank's counter
+ * has reached this epoch (bounded wait: after about a second it sets error bit 6
+ * and returns), copies buffer (e & 1) into dst (data_bytes, the assembled
+ * output) and advances the epoch.  Two buffers alternate so a rank that runs
+ * ahead never overwrites the data another rank may still be reading.  Every rank
+ * must make the same sequence of calls with the same sizes; src_bytes,
+ * dst_offset and data_bytes are multiples of 16 and src / dst 16-byte aligned.
+ * Plain peer stores and atomics only: no multicast objects. */
+#define KITTY_TP_MAX_RANKS 8
+typedef struct {
+  int32_t world;                       /* ranks taking part, 1..KITTY_TP_MAX_RANKS */
+  int32_t rank;                        /* this rank */
+  void* region[KITTY_TP_MAX_RANKS];    /* every rank's region as mapped in this process (own included) */
+  uint64_t data_bytes;                 /* bytes of one assembled output (one buffer) */
+  const void* src;                     /* this rank's slice (device memory) */
+  uint64_t src_bytes;
+  uint64_t dst_offset;                 /* where the slice goes in the assembled output */
+  void* dst;                           /* the assembled output of this call (data_bytes) */
+} KittyTpGatherArgs;
+
+/* Bytes of an exchange region for data_bytes of assembled output. */
+size_t kitty_tp_region_bytes(uint64_t data_bytes);
+/* cudaMalloc a zeroed exchange region of kitty_tp_region_bytes(data_bytes) on the
+ * current device. */
+int kitty_tp_region_alloc(uint64_t data_bytes, void** region);
+int kitty_tp_region_free(void* region);
+/* CUDA IPC handle (64 bytes into handle) of a region of this process, and the
+ * mapping of another process's region into this one (and its release). */
+int kitty_tp_ipc_handle(void* region, void* handle);
+int kitty_tp_ipc_open(const void* handle, void** region);
+int kitty_tp_ipc_close(void* region);
+int kitty_tp_allgather(const KittyTpGatherArgs* args, void* stream);
 
 /* Test and benchmark hook, no counterpart in the reference: pin the decode
  * kernel family used by later kitty_paged_decode / _workspace_size / _noalloc

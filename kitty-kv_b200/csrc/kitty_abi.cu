@@ -13,6 +13,7 @@ int quantize_value_pages_impl(const KittyValueQuantArgs* a, void* stream);
 int dequantize_key_pages_impl(const KittyKeyDequantArgs* a, void* stream);
 int dequantize_value_pages_impl(const KittyValueDequantArgs* a, void* stream);
 int read_cache_error(uint32_t* flags, int clear);
+int read_tp_error(uint32_t* flags, int clear);
 
 namespace {
 thread_local std::string g_last_error;
@@ -138,6 +139,7 @@ size_t kitty_args_size(int kind) {
     case 4: return sizeof(KittyCacheState);
     case 5: return sizeof(KittyPrefillArgs);
     case 6: return sizeof(KittyValueDequantArgs);
+    case 7: return sizeof(KittyTpGatherArgs);
     default: return 0;
   }
 }
@@ -165,14 +167,16 @@ int kitty_dequantize_value_pages(const KittyValueDequantArgs* args, void* stream
 int kitty_device_error_flags(uint32_t* flags, int clear) {
   clear_error();
   if (!flags) return fail(KITTY_ERR_INVALID_ARGUMENT, "device_error_flags: flags is NULL");
-  uint32_t b = 0, c = 0, d = 0;
+  uint32_t b = 0, c = 0, d = 0, t = 0;
   int rc = read_decode_error_i8(&b, clear);
   if (rc != KITTY_OK) return rc;
   rc = read_decode_error_tc(&d, clear);
   if (rc != KITTY_OK) return rc;
   rc = read_cache_error(&c, clear);
   if (rc != KITTY_OK) return rc;
-  *flags = b | c | d;
+  rc = read_tp_error(&t, clear);
+  if (rc != KITTY_OK) return rc;
+  *flags = b | c | d | t;
   return KITTY_OK;
 }
 

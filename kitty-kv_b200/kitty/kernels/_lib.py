@@ -16,7 +16,7 @@ from typing import Dict, Optional, Tuple
 
 import torch
 
-ABI_VERSION = 4
+ABI_VERSION = 5
 LIB_NAME = "libkitty_b200.so"
 _LIB_PATH = Path(os.environ.get("KITTY_B200_LIB", Path(__file__).resolve().parent.parent / LIB_NAME))
 
@@ -95,6 +95,14 @@ class PrefillArgs(ctypes.Structure):
                 ("page_off", c_ptr), ("page_dst", c_ptr), ("seq_plan", c_ptr)]
 
 
+TP_MAX_RANKS = 8
+
+
+class TpGatherArgs(ctypes.Structure):
+    _fields_ = [("world", c_i32), ("rank", c_i32), ("region", c_ptr * TP_MAX_RANKS), ("data_bytes", ctypes.c_uint64),
+                ("src", c_ptr), ("src_bytes", ctypes.c_uint64), ("dst_offset", ctypes.c_uint64), ("dst", c_ptr)]
+
+
 # Every symbol the header declares, with its ctypes signature.
 SIGNATURES = {
     "kitty_abi_version": (ctypes.c_int, []),
@@ -115,9 +123,16 @@ SIGNATURES = {
                                           c_ptr, c_i64, c_i64, c_ptr]),
     "kitty_cache_prefill": (ctypes.c_int, [ctypes.POINTER(CacheState), ctypes.POINTER(PrefillArgs), c_ptr]),
     "kitty_cache_release": (ctypes.c_int, [ctypes.POINTER(CacheState), c_i32, c_ptr, c_ptr]),
+    "kitty_tp_region_bytes": (c_size, [ctypes.c_uint64]),
+    "kitty_tp_region_alloc": (ctypes.c_int, [ctypes.c_uint64, ctypes.POINTER(c_ptr)]),
+    "kitty_tp_region_free": (ctypes.c_int, [c_ptr]),
+    "kitty_tp_ipc_handle": (ctypes.c_int, [c_ptr, c_ptr]),
+    "kitty_tp_ipc_open": (ctypes.c_int, [c_ptr, ctypes.POINTER(c_ptr)]),
+    "kitty_tp_ipc_close": (ctypes.c_int, [c_ptr]),
+    "kitty_tp_allgather": (ctypes.c_int, [ctypes.POINTER(TpGatherArgs), c_ptr]),
 }
 STRUCTS = {0: KeyQuantArgs, 1: ValueQuantArgs, 2: KeyDequantArgs, 3: DecodeArgs, 4: CacheState, 5: PrefillArgs,
-           6: ValueDequantArgs}
+           6: ValueDequantArgs, 7: TpGatherArgs}
 
 _lib: Optional[ctypes.CDLL] = None
 _lock = threading.Lock()

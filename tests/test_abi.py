@@ -70,12 +70,14 @@ int main(void) {
     (any_fn)kitty_dequantize_value_pages,
     (any_fn)kitty_paged_decode_workspace_size, (any_fn)kitty_paged_decode, (any_fn)kitty_paged_decode_noalloc,
     (any_fn)kitty_device_error_flags, (any_fn)kitty_decode_force_variant, (any_fn)kitty_cache_reset,
-    (any_fn)kitty_cache_append, (any_fn)kitty_cache_prefill, (any_fn)kitty_cache_release};
+    (any_fn)kitty_cache_append, (any_fn)kitty_cache_prefill, (any_fn)kitty_cache_release,
+    (any_fn)kitty_tp_region_bytes, (any_fn)kitty_tp_region_alloc, (any_fn)kitty_tp_region_free,
+    (any_fn)kitty_tp_ipc_handle, (any_fn)kitty_tp_ipc_open, (any_fn)kitty_tp_ipc_close, (any_fn)kitty_tp_allgather};
   if (kitty_abi_version() != KITTY_ABI_VERSION) return 1;
   if (kitty_args_size(0) != sizeof(KittyKeyQuantArgs) || kitty_args_size(1) != sizeof(KittyValueQuantArgs) ||
       kitty_args_size(2) != sizeof(KittyKeyDequantArgs) || kitty_args_size(3) != sizeof(KittyDecodeArgs) ||
       kitty_args_size(4) != sizeof(KittyCacheState) || kitty_args_size(5) != sizeof(KittyPrefillArgs) ||
-      kitty_args_size(6) != sizeof(KittyValueDequantArgs))
+      kitty_args_size(6) != sizeof(KittyValueDequantArgs) || kitty_args_size(7) != sizeof(KittyTpGatherArgs))
     return 2;
   KittyDecodeArgs a;
   memset(&a, 0, sizeof(a));
@@ -83,6 +85,12 @@ int main(void) {
   if (kitty_paged_decode(&a, NULL) != KITTY_ERR_INVALID_ARGUMENT) return 3;
   if (strlen(kitty_last_error()) == 0) return 4;
   if (kitty_cache_append(NULL, 0, NULL, NULL, 0, 0, NULL, 0, 0, NULL) != KITTY_ERR_INVALID_ARGUMENT) return 5;
+  if (kitty_tp_region_bytes(1024) != 2 * 1024 + 256) return 6;
+  if (kitty_tp_allgather(NULL, NULL) != KITTY_ERR_INVALID_ARGUMENT) return 7;
+  KittyTpGatherArgs t;
+  memset(&t, 0, sizeof(t));
+  t.world = 9;
+  if (kitty_tp_allgather(&t, NULL) != KITTY_ERR_INVALID_ARGUMENT) return 8;
   printf("%d entry points\n", (int)(sizeof(fns) / sizeof(fns[0])));
   return 0;
 }
