@@ -942,7 +942,7 @@ def main():
     ap.add_argument("--variant", choices=["auto", "simt", "int8", "tc"], default="auto",
                     help="decode kernel family (auto: integer tensor-core kernel for head_dim = group = 128, "
                          "CUDA-core kernel otherwise)")
-    ap.add_argument("--gather", choices=["p2p", "nccl"], default="nccl",
+    ap.add_argument("--gather", choices=["p2p", "nccl"], default="p2p",
                     help="tensor-parallel output exchange (config 4 on several GPUs): direct NVLink stores "
                          "into every rank's exchange region, or an NCCL all-gather")
     ap.add_argument("--pages-only", action="store_true",
