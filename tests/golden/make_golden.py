@@ -505,13 +505,16 @@ def run_bf16_sets(ref, rng, store, manifest):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default=os.environ.get("KITTY_REFERENCE", "/root/reference"))
+    ap.add_argument("--reference", default=os.environ.get("KITTY_REFERENCE"),
+                    help="checkout of the reference project (default: $KITTY_REFERENCE)")
     ap.add_argument("--skip-quant", action="store_true")
     ap.add_argument("--bf16-only", action="store_true",
                     help="add the bfloat16 sets to the existing golden files and keep everything else")
     ap.add_argument("--nonfinite-only", action="store_true",
                     help="add the non-finite key / value pages to the existing golden files")
     args = ap.parse_args()
+    if not args.reference:
+        ap.error("give --reference or set KITTY_REFERENCE")
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     ref = load_reference(Path(args.reference))
     if args.nonfinite_only:
