@@ -1,5 +1,6 @@
 // Paged GQA decode attention with integer tensor-core contractions
-// (head_dim = group = 128, up to 8 query heads per KV head).
+// (head_dim = group = 128; up to 8 query heads per KV head per launch, more in
+// passes of 8 that share the workspace).
 //
 // Work decomposition: segments (sequence, KV head) of items (the fp16 sinks + tail
 // in up to four chunk items, then the quantised pages), one contiguous slice of
@@ -30,6 +31,11 @@
 // integer multiply-add: no exchange between lanes, and after the key
 // contraction lane (g_, q_) owns the 16 scores of query head q_ for the tokens
 // 32 k + 4 g_ + i (k, i = 0..3; the same 16 channels of the value accumulator).
+// With 8 query heads (two groups of 4 per lane: q_ and q_ + 4) the top key digit
+// is stored signed, b2 - 64 (u8 x s8 MMA), which makes the all-ones column
+// unnecessary: one MMA per code plane then holds the b2 sums of both groups, its
+// column g_ carrying query head (g_ >> 1) + 4 (g_ & 1) so that a lane receives
+// those of its own two heads (3 key MMAs per plane and half instead of 4).
 //
 // Operand layout.  Both planes are stored with the packed dimension along a row
 // (key row = channel, 4 tokens per byte; value row = token, 4 channels per byte)
