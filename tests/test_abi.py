@@ -57,6 +57,36 @@ def test_null_args_are_rejected_without_a_gpu():
     assert b"multiple" in lib.kitty_last_error()
 
 
+def test_tp_allgather_argument_checks_without_a_gpu():
+    """kitty_tp_allgather rejects bad rank counts, missing or unaligned regions and
+    slices that do not fit, before touching the device."""
+    lib = _lib.load()
+    assert lib.kitty_tp_region_bytes(1 << 20) == 2 * (1 << 20) + 256
+    assert lib.kitty_tp_region_bytes(1000) == 2 * 1024 + 256     # buffers rounded to 256 bytes
+
+    def args(**kw):
+        a = _lib.TpGatherArgs()
+        a.world, a.rank, a.data_bytes, a.src_bytes, a.dst_offset = 2, 0, 4096, 2048, 0
+        a.src, a.dst = 0x1000, 0x2000
+        a.region[0], a.region[1] = 0x10000, 0x20000
+        for k, v in kw.items():
+            setattr(a, k, v)
+        return a
+
+    cases = [dict(world=0), dict(world=9), dict(rank=2), dict(rank=-1), dict(src=0), dict(dst=0x2004),
+             dict(data_bytes=4100), dict(src_bytes=0), dict(dst_offset=3072), dict(dst_offset=8)]
+    for kw in cases:
+        assert lib.kitty_tp_allgather(args(**kw), None) == 1, kw
+        assert lib.kitty_last_error() != b""
+    a = args()
+    a.region[1] = 0x20010                                    # not 256-byte aligned
+    assert lib.kitty_tp_allgather(a, None) == 1
+    a.region[1] = 0
+    assert lib.kitty_tp_allgather(a, None) == 1
+    assert lib.kitty_tp_region_alloc(0, ctypes.byref(_lib.c_ptr())) == 1
+    assert lib.kitty_tp_ipc_handle(None, None) == 1
+
+
 C_PROGRAM = r"""
 #include <stdio.h>
 #include <string.h>
